@@ -1,0 +1,206 @@
+// ref_shim.cpp — extern "C" entry points into the REFERENCE's own functions.
+//
+// TEST INFRASTRUCTURE ONLY.  oracle/Makefile compiles this file together with
+// the reference's sources where they lie (src/*.cpp of
+// tundefund0-gif/pocketforge) into oracle/_ref/libpfref.so.  The pin tests use
+// it to check the CPU restatement (oracle/pf_oracle.cpp) bit for bit, and
+// `bench.py --impl reference` times it.  Nothing in pocketforge_b200/ links it.
+//
+// MTPHeads keeps its weights private; D8 injects seeded weights into both
+// sides, so this translation unit reads them with `private` redefined.
+#include <cstdint>
+#include <cstring>
+#include <functional>
+#include <memory>
+#include <string>
+#include <vector>
+#include <unordered_map>
+#include <thread>
+#include <mutex>
+#include <condition_variable>
+#include <atomic>
+#include <queue>
+#include <random>
+
+#define private public
+#include "forge/mtp.hpp"
+#include "forge/engine.hpp"
+#undef private
+#include "forge/kv_cache.hpp"
+#include "forge/layer_skip.hpp"
+#include "forge/matmul_neon.hpp"
+#include "forge/quant_format.hpp"
+
+namespace forge {
+void pf_ref_seed_sampler(unsigned s);
+}
+
+extern "C" {
+
+void pfref_quantize_activation_row(const float* s, int8_t* d, float* sc, uint32_t n) {
+    forge::quantize_activation_row(s, d, sc, n);
+}
+void pfref_dequant_q4_to_int8(const uint8_t* s, int8_t* d, uint32_t n) { forge::dequant_q4_to_int8(s, d, 1.0f, n); }
+void pfref_dequant_q2_to_int8(const uint8_t* s, int8_t* d, uint32_t n) { forge::dequant_q2_to_int8(s, d, 1.0f, n); }
+void pfref_dequant_ternary_to_int8(const uint8_t* s, int8_t* d, uint32_t n) { forge::dequant_ternary_to_int8(s, d, n); }
+void pfref_matmul_int8(const int8_t* A, const int8_t* B, int32_t* C, uint32_t M, uint32_t N, uint32_t K) {
+    forge::matmul_int8(A, B, C, M, N, K);
+}
+void pfref_matmul_quantized(const float* A, const int8_t* B, float* C, uint32_t M, uint32_t N, uint32_t K,
+                            const float* ws, const float* as) {
+    forge::matmul_quantized(A, B, C, M, N, K, ws, as);
+}
+void pfref_rmsnorm(float* out, const float* x, const float* w, uint32_t n) { forge::rmsnorm(out, x, w, n); }
+void pfref_softmax(float* v, uint32_t n) { forge::softmax(v, n); }
+float pfref_dot_product(const float* a, const float* b, uint32_t n) { return forge::dot_product(a, b, n); }
+
+// ---- KVCache ----
+void* pfref_kv_create(uint32_t L, uint32_t H, uint32_t hd, uint32_t sink, uint32_t window, uint32_t pool,
+                      uint32_t max_ctx) {
+    forge::KVCacheConfig c;
+    c.n_layers = L;
+    c.n_kv_heads = H;
+    c.head_dim = hd;
+    c.sink_size = sink;
+    c.window_size = window;
+    c.pool_block = pool;
+    c.max_context = max_ctx;
+    return new forge::KVCache(c);
+}
+void pfref_kv_destroy(void* c) { delete (forge::KVCache*)c; }
+void pfref_kv_store(void* c, uint32_t l, uint32_t h, uint32_t pos, const float* k, const float* v) {
+    ((forge::KVCache*)c)->store(l, h, pos, k, v);
+}
+uint32_t pfref_kv_scores(void* c, uint32_t l, uint32_t h, const float* q, float* out) {
+    return ((forge::KVCache*)c)->attention_scores(l, h, q, out);
+}
+void pfref_kv_weighted_sum(void* c, uint32_t l, uint32_t h, const float* p, float* out, uint32_t cnt) {
+    ((forge::KVCache*)c)->attention_weighted_sum(l, h, p, out, cnt);
+}
+uint32_t pfref_kv_size(void* c) { return ((forge::KVCache*)c)->size(); }
+uint64_t pfref_kv_memory(void* c) { return ((forge::KVCache*)c)->memory_usage(); }
+
+// ---- LayerSkipController ----
+void* pfref_skip_create(uint32_t L, uint32_t d, float thr, uint32_t interval) {
+    forge::ModelConfig c;
+    c.n_layers = L;
+    c.n_embd = d;
+    c.skip_threshold = thr;
+    c.skip_interval = interval;
+    return new forge::LayerSkipController(c);
+}
+void pfref_skip_destroy(void* s) { delete (forge::LayerSkipController*)s; }
+int pfref_skip_should_skip(void* s, uint32_t l, const float* x, uint32_t n) {
+    return ((forge::LayerSkipController*)s)->should_skip_ffn(l, x, n) ? 1 : 0;
+}
+void pfref_skip_record(void* s, uint32_t l, const float* x, uint32_t n) {
+    ((forge::LayerSkipController*)s)->record_layer_output(l, x, n);
+}
+void pfref_skip_new_token(void* s) { ((forge::LayerSkipController*)s)->new_token(); }
+int pfref_skip_is_anchor(void* s) { return ((forge::LayerSkipController*)s)->is_anchor_token() ? 1 : 0; }
+uint32_t pfref_skip_total(void* s) { return ((forge::LayerSkipController*)s)->total_skipped(); }
+void pfref_skip_reset(void* s) { ((forge::LayerSkipController*)s)->reset(); }
+void pfref_skip_set_threshold(void* s, float t) { ((forge::LayerSkipController*)s)->set_threshold(t); }
+
+// ---- MTPHeads ----
+void* pfref_mtp_create(uint32_t heads, uint32_t d, uint32_t vocab) {
+    forge::MTPConfig c;
+    c.n_mtp_heads = heads;
+    c.n_embd = d;
+    c.n_vocab = vocab;
+    c.mtp_ff_dim = d;
+    return new forge::MTPHeads(c);
+}
+void pfref_mtp_destroy(void* m) { delete (forge::MTPHeads*)m; }
+void pfref_mtp_set_head(void* mp, uint32_t h, const uint8_t* g, const float* gs, const uint8_t* u, const float* us,
+                        const uint8_t* dn, const float* ds) {
+    auto* m = (forge::MTPHeads*)mp;
+    const size_t d = m->cfg_.n_embd, mb = d * (d / 2);
+    auto& w = m->heads_[h];
+    w.gate_q4.assign(g, g + mb);
+    w.up_q4.assign(u, u + mb);
+    w.down_q4.assign(dn, dn + mb);
+    w.gate_scale.assign(gs, gs + d);
+    w.up_scale.assign(us, us + d);
+    w.down_scale.assign(ds, ds + d);
+}
+void pfref_mtp_forward(void* mp, const float* hidden, const float* emb, uint64_t emb_n, float* logits) {
+    auto* m = (forge::MTPHeads*)mp;
+    std::vector<float> table(emb, emb + emb_n);
+    auto out = m->forward(hidden, table);
+    const size_t V = m->cfg_.n_vocab;
+    for (size_t h = 0; h < out.size(); h++) std::memcpy(logits + h * V, out[h].data(), V * sizeof(float));
+}
+void pfref_mtp_quantize_q4(const float* src, uint8_t* dst, float* scales, uint32_t rows, uint32_t cols) {
+    std::vector<float> s;
+    forge::MTPHeads::quantize_q4(src, dst, s, rows, cols);
+    std::memcpy(scales, s.data(), rows * sizeof(float));
+}
+int32_t pfref_mtp_argmax(const float* v, uint32_t n) { return forge::MTPHeads::argmax(v, n); }
+int pfref_mtp_speculative_accept(void* mp, int32_t token, const float* logits, uint32_t heads) {
+    auto* m = (forge::MTPHeads*)mp;
+    const size_t V = m->cfg_.n_vocab;
+    std::vector<std::vector<float>> l(heads);
+    for (uint32_t h = 0; h < heads; h++) l[h].assign(logits + h * V, logits + (h + 1) * V);
+    return m->speculative_accept(token, l);
+}
+
+// ---- Quantizer / WeightLoader ----
+uint64_t pfref_quantize_matrix(const float* data, uint32_t rows, uint32_t cols, int qtype, uint8_t* out) {
+    forge::ModelConfig c;
+    forge::Quantizer q(c);
+    auto v = q.quantize_matrix(data, rows, cols, (uint8_t)qtype);
+    if (out) std::memcpy(out, v.data(), v.size());
+    return v.size();
+}
+// Writes a one-block .squeeze with the reference Quantizer (zstd-compressed)
+// and reads it back through WeightLoader::load_block_with_scales.
+int pfref_squeeze_roundtrip(const char* path, const float* data, uint32_t rows, uint32_t cols, int qtype,
+                            int8_t* out, float* row_scales, float* global_scale) {
+    forge::ModelConfig c;
+    c.n_layers = 1;
+    forge::Quantizer q(c);
+    auto qd = q.quantize_matrix(data, rows, cols, (uint8_t)qtype);
+    auto comp = q.compress_block(qd);
+    forge::WeightBlock b{};
+    b.layer_id = 0;
+    b.matrix_id = 4;
+    b.n_rows = rows;
+    b.n_cols = cols;
+    b.compressed_size = (uint32_t)comp.size();
+    b.original_size = (uint32_t)qd.size();
+    b.quant_type = (uint8_t)qtype;
+    b.offset = 0;
+    if (!q.write_squeeze(path, {b}, {comp}, c)) return -1;
+    forge::WeightLoader ld;
+    if (!ld.open(path)) return -2;
+    auto r = ld.load_block_with_scales(0, 4);
+    if (r.data.size() != (size_t)rows * cols) return -3;
+    std::memcpy(out, r.data.data(), r.data.size());
+    std::memcpy(row_scales, r.row_scales.data(), r.row_scales.size() * sizeof(float));
+    *global_scale = r.global_scale;
+    return 0;
+}
+
+// ---- Engine sampling (src/engine.cpp:881-1003) ----
+void* pfref_engine_create(void) { return new forge::Engine(); }
+void pfref_engine_destroy(void* e) { delete (forge::Engine*)e; }
+void pfref_seed_sampler(uint32_t s) { forge::pf_ref_seed_sampler(s); }
+int32_t pfref_sample(void* e, const float* lg, uint32_t n, float temperature, float top_p, uint32_t top_k,
+                     int greedy) {
+    forge::SamplingConfig c;
+    c.temperature = temperature;
+    c.top_p = top_p;
+    c.top_k = top_k;
+    c.greedy = greedy != 0;
+    return ((forge::Engine*)e)->sample(lg, n, c);
+}
+int32_t pfref_sample_greedy(void* e, const float* lg, uint32_t n) { return ((forge::Engine*)e)->sample_greedy(lg, n); }
+int32_t pfref_sample_top_p(void* e, const float* lg, uint32_t n, float p, float t) {
+    return ((forge::Engine*)e)->sample_top_p(lg, n, p, t);
+}
+int32_t pfref_sample_top_k(void* e, const float* lg, uint32_t n, uint32_t k, float t) {
+    return ((forge::Engine*)e)->sample_top_k(lg, n, k, t);
+}
+
+}  // extern "C"
