@@ -1,0 +1,308 @@
+#!/usr/bin/env python
+"""Benchmark of the batched MTP speculative-decode step (one JSON line).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config config2] [--impl ours|reference]
+
+A step is one speculative-decode step of every sequence on a GPU: K+1 verify
+rows per sequence through the 22-layer Q4 model over the 3-tier int8 KV cache,
+greedy acceptance, KV commit, and K new MTP drafts.  Default workload is the
+batch-64, K=4 configuration (config2 of BASELINE.json) with a synthetic
+random-init model (weights N(0,0.02) seed 0 through the reference's Quantizer
+and loader; MTP heads seed 3) and uniform-random 512-token prompts.
+
+Multi-GPU (torchrun, one rank per GPU): every rank holds a full replica and
+its own 64 sequences (weak scaling, no collective in the step); the timed
+region is bracketed by barriers and device synchronisation and the slowest
+rank's device time is used.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "accepted tok/s"
+UNIT = "tok/s"
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.out = ""
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                self.out = ""
+
+    def summary(self):
+        rows = [r.split(", ") for r in self.out.strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for name, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def make_prompts(n, length, vocab, seed):
+    rng = np.random.default_rng(seed)
+    return [rng.integers(0, vocab, length).astype(np.int32) for _ in range(n)]
+
+
+def kv_entry_bytes(model):
+    return model.n_layers * model.n_kv_heads * (2 * model.head_dim + 8)
+
+
+def algorithmic_bytes_per_step(model, n_seqs, ctx_avg, committed_per_step, K):
+    """Bytes a verify step must move (weights, LM head, MTP heads, attended
+    int8 KV, committed KV writes); activations stay on chip / in L2."""
+    W = model.weight_bytes()
+    E = model.n_vocab * model.n_embd // 2 if model.emb_qtype == 1 else model.n_vocab * model.n_embd
+    H = K * 3 * model.n_embd * model.n_embd // 2 + K * 3 * model.n_embd * 4
+    kv_read = n_seqs * ctx_avg * kv_entry_bytes(model)
+    kv_write = committed_per_step * kv_entry_bytes(model)
+    return W + E + H + kv_read + kv_write
+
+
+def cpu_baseline(model, seconds_budget=25.0, threads=8):
+    """The oracle port (CPU restatement of the Level-B step, one core) on a
+    bounded sample: 1 sequence, 4-token prompt, decode steps until ~budget."""
+    import ctypes as C
+
+    import oracle
+    from oracle import PfModelConfig
+    L = oracle.lib()
+    c = PfModelConfig()
+    for name, _ in PfModelConfig._fields_:
+        if name == "qtype":
+            for i, q in enumerate(model.qtype):
+                c.qtype[i] = q
+        else:
+            setattr(c, name, type(getattr(c, name))(getattr(model, name)))
+    e = L.po_engine_create(C.byref(c))
+    try:
+        L.po_engine_load_synthetic(e, 0, 3, threads)
+        toks = np.arange(4, dtype=np.int32)
+        L.po_engine_prefill(e, 1, toks, np.array([0, 4], np.int64), None)
+        n = np.zeros(1, np.int32)
+        em = np.zeros(model.n_mtp_heads + 1, np.int32)
+        gen, steps, t0 = 0, 0, time.perf_counter()
+        while True:
+            L.po_engine_step(e, n.ctypes.data, em.ctypes.data)
+            gen += int(n[0])
+            steps += 1
+            el = time.perf_counter() - t0
+            if el > seconds_budget or steps >= 8:
+                break
+        return {"value": gen / el, "unit": UNIT, "cores": 1, "kind": "port",
+                "sample": f"oracle port (oracle/pf_oracle.cpp, -O2, 1 thread): 1 sequence, 4-token prompt, "
+                          f"{steps} decode steps, {gen} tokens in {el:.1f} s on the full 1B model"}
+    finally:
+        L.po_engine_destroy(e)
+
+
+def reference_arm(args):
+    """The reference's own CPU implementation (oracle/_ref, compiled from its
+    sources) on the host cores."""
+    import multiprocessing as mp
+    import oracle
+    if not oracle.ref_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libpfref.so not built"}))
+        return
+    from oracle import refbench
+    import pocketforge_b200 as pf
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    out = refbench.run(args, cores, pf.PRESETS[args.config]["model"])
+    print(json.dumps(out))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=4)
+    ap.add_argument("--config", default="config2")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--seqs", type=int, default=0, help="override sequences per GPU")
+    ap.add_argument("--prompt", type=int, default=0, help="override prompt length")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank == 0:
+            reference_arm(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import pocketforge_b200 as pf
+
+    if world > 1:
+        torch.cuda.set_device(local)
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    preset = pf.PRESETS[args.config]
+    model = preset["model"]
+    seqs = args.seqs or preset["seqs"]
+    plen = args.prompt or preset["prompt"]
+    K = model.n_mtp_heads
+    R = K + 1
+    max_pos = plen + (args.warmup + args.steps + 2) * R + 8
+    if model.max_context < max_pos:
+        max_pos = model.max_context
+    eng = pf.BatchEngine(model, seqs, max_pos, device=local)
+    eng.load_synthetic(seed=0, mtp_seed=3, threads=7)
+    sampling = preset.get("sampling")
+    if sampling:
+        eng.set_sampling(sampling["temperature"], sampling["top_p"], sampling["top_k"], False)
+    prompts = make_prompts(seqs, plen, model.n_vocab, seed=1 + 1000003 * rank)
+    seeds = [sampling["seed"] + rank * seqs + i for i in range(seqs)] if sampling else None
+
+    # ---- end to end through the public API: pinned host prompts -> prefill
+    # -> steps with every step's tokens read back to the host.
+    e2e = None
+    if not args.no_e2e:
+        pinned = torch.from_numpy(np.concatenate(prompts)).pin_memory()
+        host_prompts = np.split(pinned.numpy(), seqs)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        eng.prefill(host_prompts, seeds)
+        got = seqs  # the first token comes out of prefill
+        for _ in range(args.steps):
+            n, em = eng.step()
+            got += int(n.sum())
+        torch.cuda.synchronize()
+        el = time.perf_counter() - t0
+        if world > 1:
+            t = torch.tensor([el, got], dtype=torch.float64, device="cuda")
+            mx = t.clone()
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+            dist.all_reduce(t, op=dist.ReduceOp.SUM)
+            el, got = float(mx[0]), float(t[1])
+        e2e = {"value": got / el, "unit": UNIT,
+               "h2d_bytes_per_step": int(seqs * plen * 4 / max(1, args.steps)),
+               "d2h_bytes_per_step": int(seqs * (R + 1) * 4),
+               "includes": f"prefill of {seqs}x{plen} prompt tokens from pinned host memory + {args.steps} "
+                           f"pf_engine_step calls, each reading the step's tokens back to the host"}
+
+    # ---- device-resident timing
+    eng.prefill(prompts, seeds)
+    eng.run_steps(args.warmup)
+    pos0 = eng.read_positions().astype(np.int64)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        ms = eng.run_steps(args.steps)
+    torch.cuda.synchronize()
+    pos1 = eng.read_positions().astype(np.int64)
+    tokens = int((pos1 - pos0).sum())
+    launches = eng.launches_per_step() * args.steps
+    if world > 1:
+        t = torch.tensor([ms, tokens], dtype=torch.float64, device="cuda")
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        ms_max, tokens_all = float(mx[0]), int(t[1])
+    else:
+        ms_max, tokens_all = ms, tokens
+    step_ms = ms / args.steps
+    ctx_avg = float(((pos0 + pos1) / 2).mean())
+    committed = (pos1 - pos0).sum() / args.steps
+    bytes_step = algorithmic_bytes_per_step(model, seqs, ctx_avg, committed, K)
+    peak, peak_kind = load_peaks()
+    achieved = bytes_step / (step_ms * 1e-3) / 1e9
+    clocks = clk.summary()
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(model)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": tokens_all / (ms_max * 1e-3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic",
+            "config": {"workload": f"{args.config}: {seqs} sequences/GPU x {plen}-token uniform-random prompts, "
+                                   f"MTP K={K} {'stochastic' if sampling else 'greedy'} verify of M={seqs * R} "
+                                   f"rows/step, 1B Q4 model (22L, d2048, 32/8 heads, ffn 5632, vocab 16384)",
+                       "seqs_per_gpu": seqs, "global_seqs": seqs * world, "prompt": plen,
+                       "context_avg": ctx_avg, "window": model.window_size,
+                       "l2": "no flush: weights (0.52 GB) + KV read per step exceed the 126 MB L2",
+                       "parallelism": f"replicas x{world}"},
+            "verify_step_us": step_ms * 1e3,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
+                         "unit_of_work": "one decode step (CUDA graph launch)",
+                         "algorithmic_bytes_per_step": bytes_step},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "clocks": clocks,
+            "gpu_launches": launches,
+        }
+        print(json.dumps(line))
+    eng.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

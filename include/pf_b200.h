@@ -29,6 +29,12 @@
 extern "C" {
 #endif
 
+#if defined(__GNUC__)
+#define PF_API __attribute__((visibility("default")))
+#else
+#define PF_API
+#endif
+
 typedef int32_t pf_status;
 enum {
     PF_OK = 0,
@@ -85,11 +91,11 @@ typedef struct pf_sampling_config {
 /* ------------------------------------------------------------------ */
 /* Library                                                              */
 /* ------------------------------------------------------------------ */
-const char* pf_last_error(void);
+PF_API const char* pf_last_error(void);
 /* Number of visible devices with compute capability 10.x (0 when none). */
-int32_t pf_device_count(void);
+PF_API int32_t pf_device_count(void);
 /* Bytes of one packed weight matrix on the device for a format. */
-size_t pf_packed_weight_bytes(int32_t rows, int32_t cols, int32_t qtype);
+PF_API size_t pf_packed_weight_bytes(int32_t rows, int32_t cols, int32_t qtype);
 
 /* ------------------------------------------------------------------ */
 /* Kernel-level entry points (device pointers, caller-owned)            */
@@ -97,48 +103,48 @@ size_t pf_packed_weight_bytes(int32_t rows, int32_t cols, int32_t qtype);
 
 /* forge::quantize_activation_row (include/forge/matmul_neon.hpp:20-25),
  * applied to each of M rows of x[M][K]: q[M][K] int8, scales[M]. */
-pf_status pf_quantize_activation_rows(const float* x, int8_t* q, float* scales,
+PF_API pf_status pf_quantize_activation_rows(const float* x, int8_t* q, float* scales,
                                       int32_t M, int32_t K, void* stream);
 
 /* forge::dequant_q4_to_int8 / dequant_q2_to_int8 / dequant_ternary_to_int8
  * (include/forge/matmul_neon.hpp:28-48). `scale` is ignored, as in the
  * reference (src/matmul_neon.cpp:37,53). */
-pf_status pf_dequant_q4_to_int8(const uint8_t* src, int8_t* dst, float scale,
+PF_API pf_status pf_dequant_q4_to_int8(const uint8_t* src, int8_t* dst, float scale,
                                 int64_t n, void* stream);
-pf_status pf_dequant_q2_to_int8(const uint8_t* src, int8_t* dst, float scale,
+PF_API pf_status pf_dequant_q2_to_int8(const uint8_t* src, int8_t* dst, float scale,
                                 int64_t n, void* stream);
-pf_status pf_dequant_ternary_to_int8(const uint8_t* src, int8_t* dst,
+PF_API pf_status pf_dequant_ternary_to_int8(const uint8_t* src, int8_t* dst,
                                      int64_t n, void* stream);
 
 /* forge::matmul_int8 (include/forge/matmul_neon.hpp:55-62):
  * C[M][N] (int32) = A[M][K] (int8) . B[N][K]^T (int8). */
-pf_status pf_matmul_int8(const int8_t* A, const int8_t* B, int32_t* C,
+PF_API pf_status pf_matmul_int8(const int8_t* A, const int8_t* B, int32_t* C,
                          int32_t M, int32_t N, int32_t K, void* stream);
 
 /* forge::matmul_quantized (include/forge/matmul_neon.hpp:68-77):
  * C = ((float)(quant(A) . B^T) * a_scale[i]) * w_scale[j].
  * act_scales may be NULL (computed per row, as the engine always does). */
-pf_status pf_matmul_quantized(const float* A, const int8_t* B, float* C,
+PF_API pf_status pf_matmul_quantized(const float* A, const int8_t* B, float* C,
                               int32_t M, int32_t N, int32_t K,
                               const float* weight_scales, const float* act_scales,
                               void* stream);
 
 /* forge::rmsnorm (include/forge/matmul_neon.hpp:92) over M rows of n. */
-pf_status pf_rmsnorm_rows(float* out, const float* x, const float* weight,
+PF_API pf_status pf_rmsnorm_rows(float* out, const float* x, const float* weight,
                           int32_t M, int32_t n, void* stream);
 
 /* forge::softmax (include/forge/matmul_neon.hpp:87), in place over M rows. */
-pf_status pf_softmax_rows(float* vals, int32_t M, int32_t n, void* stream);
+PF_API pf_status pf_softmax_rows(float* vals, int32_t M, int32_t n, void* stream);
 
 /* Engine::sample_greedy / MTPHeads::argmax (src/engine.cpp:918-928,
  * src/mtp.cpp:145-155): first index of the maximum of each row. */
-pf_status pf_argmax_rows(const float* logits, int32_t M, int32_t n,
+PF_API pf_status pf_argmax_rows(const float* logits, int32_t M, int32_t n,
                          int32_t* out, void* stream);
 
 /* Engine::sample (src/engine.cpp:881-1003) for each row, the uniform draw of
  * row i given in uniforms[i] (host code pre-draws them from the sequence's
  * std::mt19937 exactly as the reference's uniform_real_distribution<float>). */
-pf_status pf_sample_rows(const float* logits, int32_t M, int32_t n,
+PF_API pf_status pf_sample_rows(const float* logits, int32_t M, int32_t n,
                          const pf_sampling_config* cfg, const float* uniforms,
                          int32_t* out, void* stream);
 
@@ -146,13 +152,13 @@ pf_status pf_sample_rows(const float* logits, int32_t M, int32_t n,
  * WeightLoader::load_block_with_scales, src/quant_format.cpp:348-425) into the
  * device format of `qtype` (Q4: 4-bit, Q2/Q1.5: 2-bit, Q8: 8-bit).
  * Values outside the format's range are rejected with PF_ERR_DEVICE. */
-pf_status pf_pack_weights(const int8_t* w, int32_t rows, int32_t cols,
+PF_API pf_status pf_pack_weights(const int8_t* w, int32_t rows, int32_t cols,
                           int32_t qtype, void* packed, void* stream);
 
 /* The projection kernel of the engine: C = (int32)(Aq . unpack(W)^T) with the
  * scale epilogue of matmul_quantized (src/matmul_neon.cpp:176-180):
  * C[i][j] = ((float)acc * a_scale[i]) * w_scale[j]. Aq int8 [M][K]. */
-pf_status pf_gemm_packed(const int8_t* Aq, const float* a_scale,
+PF_API pf_status pf_gemm_packed(const int8_t* Aq, const float* a_scale,
                          const void* packed_w, const float* w_scale, int32_t qtype,
                          float* C, int32_t M, int32_t N, int32_t K, void* stream);
 
@@ -164,39 +170,39 @@ pf_status pf_gemm_packed(const int8_t* Aq, const float* a_scale,
 typedef struct pf_engine pf_engine;
 
 /* max_seqs sequences of up to max_positions tokens each.  K = n_mtp_heads. */
-pf_status pf_engine_create(const pf_model_config* cfg, int32_t max_seqs,
+PF_API pf_status pf_engine_create(const pf_model_config* cfg, int32_t max_seqs,
                            int32_t max_positions, int32_t device, pf_engine** out);
-void      pf_engine_destroy(pf_engine* e);
+PF_API void      pf_engine_destroy(pf_engine* e);
 
 /* Weights (host pointers).  Layer matrices: int8 values + per-row scales as the
  * reference's WeightLoader::load_block_with_scales returns them
  * (src/quant_format.cpp:348-425). */
-pf_status pf_engine_set_matrix(pf_engine* e, int32_t layer, int32_t matrix,
+PF_API pf_status pf_engine_set_matrix(pf_engine* e, int32_t layer, int32_t matrix,
                                const int8_t* w, const float* row_scales);
 /* Tied embedding: int8 [n_vocab][n_embd] and the block's global_scale
  * (src/engine.cpp:146-165). */
-pf_status pf_engine_set_embedding(pf_engine* e, const int8_t* emb, float global_scale);
+PF_API pf_status pf_engine_set_embedding(pf_engine* e, const int8_t* emb, float global_scale);
 /* RMSNorm weights (blocks 7/8/9, src/engine.cpp:171-203); default all 1.0. */
-pf_status pf_engine_set_norms(pf_engine* e, const float* attn_norm, const float* ffn_norm,
+PF_API pf_status pf_engine_set_norms(pf_engine* e, const float* attn_norm, const float* ffn_norm,
                               const float* final_norm);
 /* One MTP head: packed Q4 nibbles + per-row scales as MTPHeads::quantize_q4
  * produces them (src/mtp.cpp:174-197). gate/up: [n_embd][n_embd/2] bytes,
  * down: [n_embd][n_embd/2] bytes. */
-pf_status pf_engine_set_mtp_head(pf_engine* e, int32_t head,
+PF_API pf_status pf_engine_set_mtp_head(pf_engine* e, int32_t head,
                                  const uint8_t* gate_q4, const float* gate_scale,
                                  const uint8_t* up_q4, const float* up_scale,
                                  const uint8_t* down_q4, const float* down_scale);
 
 /* Sampling: greedy when cfg->greedy or temperature <= 0 (src/engine.cpp:883). */
-pf_status pf_engine_set_sampling(pf_engine* e, const pf_sampling_config* cfg);
+PF_API pf_status pf_engine_set_sampling(pf_engine* e, const pf_sampling_config* cfg);
 /* Layer-skip threshold (Engine::set_layer_skip_threshold, src/engine.cpp:266-269). */
-pf_status pf_engine_set_skip_threshold(pf_engine* e, float threshold);
+PF_API pf_status pf_engine_set_skip_threshold(pf_engine* e, float threshold);
 
 /* Resets all sequences and prefills n_seqs prompts (host arrays; prompt i is
  * tokens[offsets[i] .. offsets[i+1])).  Afterwards each sequence holds its
  * first pending token and K MTP drafts.  seeds[i] seeds sequence i's
  * std::mt19937 for stochastic sampling (may be NULL when greedy). */
-pf_status pf_engine_prefill(pf_engine* e, int32_t n_seqs, const int32_t* tokens,
+PF_API pf_status pf_engine_prefill(pf_engine* e, int32_t n_seqs, const int32_t* tokens,
                             const int64_t* offsets, const uint32_t* seeds);
 
 /* One speculative-decode step for every sequence: verify the K+1 rows
@@ -204,28 +210,55 @@ pf_status pf_engine_prefill(pf_engine* e, int32_t n_seqs, const int32_t* tokens,
  * skip-cache state, emit accepted + 1 tokens, and draft K new tokens.
  * n_emitted[i] (host, may be NULL) receives accepted+1 for sequence i and
  * emitted (host, may be NULL) receives those tokens at emitted[i*(K+1)+j]. */
-pf_status pf_engine_step(pf_engine* e, int32_t* n_emitted, int32_t* emitted);
+PF_API pf_status pf_engine_step(pf_engine* e, int32_t* n_emitted, int32_t* emitted);
+
+/* Replaces the pending drafts of every sequence (host [n_seqs][K]): drafts
+ * from another proposer, or forced drafts that exercise acceptance. */
+PF_API pf_status pf_engine_set_drafts(pf_engine* e, const int32_t* drafts);
 
 /* Runs `steps` steps back to back without host synchronisation in between
  * (tokens stay on the device); for timing. */
-pf_status pf_engine_run_steps(pf_engine* e, int32_t steps);
+PF_API pf_status pf_engine_run_steps(pf_engine* e, int32_t steps);
 
 /* Copies of engine state, for tests (host destinations). */
-pf_status pf_engine_read_logits(pf_engine* e, float* out);       /* [n_seqs*(K+1)][n_vocab] of the last verify */
-pf_status pf_engine_read_drafts(pf_engine* e, int32_t* out);     /* [n_seqs][K]   */
-pf_status pf_engine_read_pending(pf_engine* e, int32_t* out);    /* [n_seqs]      */
-pf_status pf_engine_read_positions(pf_engine* e, int32_t* out);  /* [n_seqs] committed lengths */
-pf_status pf_engine_read_hidden(pf_engine* e, float* out);       /* [n_seqs][n_embd] MTP input */
-pf_status pf_engine_read_mtp_logits(pf_engine* e, float* out);   /* [n_seqs][K][n_vocab] */
-pf_status pf_engine_read_skip_counts(pf_engine* e, int64_t* computed, int64_t* skipped);
+PF_API pf_status pf_engine_read_logits(pf_engine* e, float* out);       /* [n_seqs*(K+1)][n_vocab] of the last verify */
+PF_API pf_status pf_engine_read_drafts(pf_engine* e, int32_t* out);     /* [n_seqs][K]   */
+PF_API pf_status pf_engine_read_pending(pf_engine* e, int32_t* out);    /* [n_seqs]      */
+PF_API pf_status pf_engine_read_positions(pf_engine* e, int32_t* out);  /* [n_seqs] committed lengths */
+PF_API pf_status pf_engine_read_hidden(pf_engine* e, float* out);       /* [n_seqs][n_embd] MTP input */
+PF_API pf_status pf_engine_read_mtp_logits(pf_engine* e, float* out);   /* [n_seqs][K][n_vocab] */
+PF_API pf_status pf_engine_read_skip_counts(pf_engine* e, int64_t* computed, int64_t* skipped);
+/* Every token emitted since prefill: counts[n_seqs], tokens[n_seqs][cap]. */
+PF_API pf_status pf_engine_read_log(pf_engine* e, int32_t* counts, int32_t* tokens, int32_t cap);
 /* Committed K/V of one (sequence, layer, kv_head) in the reference's logical
  * attention order (sink, pool, window): k,v int8 [count][head_dim] and
  * scales [count].  *count receives the number of entries. */
-pf_status pf_engine_read_kv(pf_engine* e, int32_t seq, int32_t layer, int32_t kv_head,
+PF_API pf_status pf_engine_read_kv(pf_engine* e, int32_t seq, int32_t layer, int32_t kv_head,
                             int8_t* k, float* k_scale, int8_t* v, float* v_scale,
                             int32_t max_entries, int32_t* count);
+/* Kernels launched by one decode step (nodes of the captured CUDA graph). */
+PF_API pf_status pf_engine_launches_per_step(pf_engine* e, int32_t* kernels);
 /* Device time of the last pf_engine_step / run_steps call, milliseconds. */
-pf_status pf_engine_last_ms(pf_engine* e, float* ms);
+PF_API pf_status pf_engine_last_ms(pf_engine* e, float* ms);
+
+/* ------------------------------------------------------------------ */
+/* Synthetic model (benchmark and test inputs; host memory)             */
+/* ------------------------------------------------------------------ */
+/* One transformer matrix as the reference's tools would produce it:
+ * N(0, 0.02) floats from a std::mt19937 seeded per (seed, layer, matrix),
+ * Quantizer::quantize_matrix (src/quant_format.cpp:44-157), then
+ * WeightLoader::load_block_with_scales (src/quant_format.cpp:348-425).
+ * The embedding is (layer 0, matrix 10). */
+PF_API pf_status pf_synth_matrix(uint32_t seed, int32_t layer, int32_t matrix, int32_t rows, int32_t cols,
+                                 int32_t qtype, int8_t* out, float* row_scales, float* global_scale);
+/* MTP matrix `which` (0 gate, 1 up, 2 down) of `head`: uniform(-1,1)/sqrt(d)
+ * floats (MTPHeads::init_weights, src/mtp.cpp:31-39) through
+ * MTPHeads::quantize_q4 (src/mtp.cpp:174-197): q4 [d][d/2], scales [d]. */
+PF_API pf_status pf_synth_mtp_matrix(uint32_t seed, int32_t head, int32_t which, int32_t d, uint8_t* q4,
+                                     float* scales);
+/* Generates every matrix of the model on `threads` host threads and loads it. */
+PF_API pf_status pf_engine_load_synthetic(pf_engine* e, const pf_model_config* cfg, uint32_t seed,
+                                          uint32_t mtp_seed, int32_t threads);
 
 #ifdef __cplusplus
 }

@@ -17,11 +17,13 @@
 //   per kv head, per-head attention output slots, greedy verification with a
 //   commit of the accepted prefix only, and K+1 verify rows [pending, drafts].
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
 #include <memory>
 #include <random>
+#include <thread>
 #include <vector>
 
 #include "../include/pf_b200.h"
@@ -1146,6 +1148,13 @@ void po_engine_read_logits(void* ep, float* out) {
     auto* e = (po::Engine*)ep;
     std::memcpy(out, e->last_logits.data(), e->last_logits.size() * sizeof(float));
 }
+// Replaces the pending drafts (drafts from another proposer; used to drive
+// the acceptance and commit paths in tests).
+void po_engine_set_drafts(void* ep, const int32_t* in) {
+    auto* e = (po::Engine*)ep;
+    for (size_t b = 0; b < e->seqs.size(); b++)
+        std::memcpy(e->seqs[b].drafts.data(), in + b * e->K(), e->K() * sizeof(int32_t));
+}
 void po_engine_read_drafts(void* ep, int32_t* out) {
     auto* e = (po::Engine*)ep;
     for (size_t b = 0; b < e->seqs.size(); b++)
@@ -1180,6 +1189,48 @@ uint32_t po_engine_read_kv(void* ep, int32_t b, uint32_t l, uint32_t h, int8_t* 
     auto* e = (po::Engine*)ep;
     return po_kv_dump(&e->seqs[b].kv, l, h, k, ks, v, vs, max_n);
 }
+// Generates (on `threads` host threads) and loads the whole synthetic model.
+void po_engine_load_synthetic(void* ep, uint32_t seed, uint32_t mtp_seed, int threads) {
+    auto* e = (po::Engine*)ep;
+    const uint32_t L = (uint32_t)e->cfg.n_layers;
+    std::vector<std::pair<uint32_t, uint32_t>> jobs;
+    for (uint32_t l = 0; l < L; l++)
+        for (uint32_t m = 0; m < PF_MAT_COUNT; m++) jobs.push_back({l, m});
+    std::atomic<size_t> next{0};
+    auto work = [&]() {
+        for (size_t j; (j = next++) < jobs.size();) {
+            const uint32_t l = jobs[j].first, m = jobs[j].second;
+            uint32_t r, c;
+            e->mat_shape((int)m, &r, &c);
+            std::vector<int8_t> w((size_t)r * c);
+            std::vector<float> rs(r);
+            float gs;
+            po::synth_matrix(seed, l, m, r, c, e->cfg.qtype[m], w.data(), rs.data(), &gs);
+            e->w[m][l] = std::move(w);
+            e->rs[m][l] = std::move(rs);
+        }
+    };
+    std::vector<std::thread> pool;
+    for (int t = 0; t < std::max(1, threads); t++) pool.emplace_back(work);
+    for (auto& t : pool) t.join();
+    const size_t V = e->cfg.n_vocab, d = e->cfg.n_embd;
+    std::vector<int8_t> emb(V * d);
+    std::vector<float> rs(V);
+    float gs;
+    po::synth_matrix(seed, 0, 10, (uint32_t)V, (uint32_t)d, e->cfg.emb_qtype, emb.data(), rs.data(), &gs);
+    po_engine_set_embedding(ep, emb.data(), gs);
+    for (int h = 0; h < e->cfg.n_mtp_heads; h++) {
+        std::vector<uint8_t> q[3];
+        std::vector<float> s[3];
+        for (int j = 0; j < 3; j++) {
+            q[j].resize(d * d / 2);
+            s[j].resize(d);
+            po::synth_mtp_matrix(mtp_seed, h, j, (uint32_t)d, q[j].data(), s[j].data());
+        }
+        po_engine_set_mtp_head(ep, h, q[0].data(), s[0].data(), q[1].data(), s[1].data(), q[2].data(), s[2].data());
+    }
+}
+
 // One token through the model for sequence b without changing its state
 // (the logits and hidden that row would produce at the next position).
 void po_engine_probe_row(void* ep, int32_t b, int32_t token, float* logits, float* hidden) {

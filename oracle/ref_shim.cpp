@@ -182,6 +182,53 @@ int pfref_squeeze_roundtrip(const char* path, const float* data, uint32_t rows, 
     return 0;
 }
 
+// ---- The literal reference engine (Engine::load_model / generate) ----
+// Writes a .squeeze whose header carries the model shape and whose only block
+// is the tied embedding (0,10), quantized by the reference Quantizer from the
+// given floats.  The reference engine never loads layer matrices
+// (Engine::load_layer_weights has no caller), so this is the complete input
+// its generate() reads.
+int pfref_write_model(const char* path, uint32_t n_layers, uint32_t d, uint32_t heads, uint32_t kv_heads,
+                      uint32_t ff, uint32_t vocab, uint32_t max_seq, uint32_t mtp_heads, const float* emb,
+                      int qtype) {
+    forge::ModelConfig c;
+    c.n_layers = n_layers;
+    c.n_embd = d;
+    c.n_heads = heads;
+    c.n_kv_heads = kv_heads;
+    c.n_ff = ff;
+    c.n_vocab = vocab;
+    c.max_seq_len = max_seq;
+    c.mtp_heads = mtp_heads;
+    forge::Quantizer q(c);
+    auto qd = q.quantize_matrix(emb, vocab, d, (uint8_t)qtype);
+    auto comp = q.compress_block(qd);
+    forge::WeightBlock b{};
+    b.layer_id = 0;
+    b.matrix_id = 10;
+    b.n_rows = vocab;
+    b.n_cols = d;
+    b.compressed_size = (uint32_t)comp.size();
+    b.original_size = (uint32_t)qd.size();
+    b.quant_type = (uint8_t)qtype;
+    return q.write_squeeze(path, {b}, {comp}, c) ? 0 : -1;
+}
+
+// Engine::generate on one prompt; returns the number of generated tokens and
+// the engine's own tokens_per_second (which counts prompt tokens).
+int pfref_literal_generate(const char* path, const int32_t* prompt, uint32_t n, uint32_t max_new, int32_t* out,
+                           float* engine_tps) {
+    forge::Engine e;
+    if (!e.load_model(path)) return -1;
+    e.set_max_memory((size_t)1 << 40);  // the 250 MB default stops a 1B model before its first token
+    std::vector<int32_t> p(prompt, prompt + n);
+    auto r = e.generate(p, max_new);
+    const size_t gen = r.tokens.size() > n ? r.tokens.size() - n : 0;
+    for (size_t i = 0; i < gen; i++) out[i] = r.tokens[n + i];
+    *engine_tps = r.tokens_per_second;
+    return (int)gen;
+}
+
 // ---- Engine sampling (src/engine.cpp:881-1003) ----
 void* pfref_engine_create(void) { return new forge::Engine(); }
 void pfref_engine_destroy(void* e) { delete (forge::Engine*)e; }

@@ -1,0 +1,394 @@
+// accept.cu — the control kernels of a speculative-decode step: building the
+// K+1 verify rows, the greedy acceptance of the drafted prefix, stochastic
+// sampling (temperature / top-k / top-p with the reference's quirks),
+// predictive FFN layer skipping, and the commit of per-sequence state.
+#include <cfloat>
+
+#include "step.cuh"
+
+namespace pf {
+
+// ---------------------------------------------------------------------------
+// Verify rows: [pending, d_0 .. d_{K-1}] at positions len .. len+K.
+// ---------------------------------------------------------------------------
+__global__ void verify_setup_kernel(int n_seqs, int K, int max_pos, const int* __restrict__ pending,
+                                    const int* __restrict__ drafts, const int* __restrict__ seq_len,
+                                    int* __restrict__ row_tok, int* __restrict__ row_pos, int* __restrict__ bs_row0,
+                                    int* __restrict__ bs_n, int* __restrict__ bs_len0, uint32_t* err) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= n_seqs) return;
+    const int R = K + 1;
+    const int len = seq_len[b];
+    const bool fits = len + R <= max_pos;
+    if (!fits) atomicOr(err, ERR_CONTEXT);
+    bs_row0[b] = b * R;
+    bs_n[b] = fits ? R : 0;
+    bs_len0[b] = len;
+    for (int r = 0; r < R; r++) {
+        row_tok[b * R + r] = (r == 0) ? pending[b] : drafts[b * K + r - 1];
+        row_pos[b * R + r] = min(len + r, max_pos - 1);
+    }
+}
+
+pf_status verify_setup(const StepBufs& s, cudaStream_t st) {
+    verify_setup_kernel<<<ceil_div(s.n_seqs, 128), 128, 0, st>>>(s.n_seqs, s.K, s.max_pos, s.pending, s.drafts,
+                                                                 s.seq_len, s.row_tok, s.row_pos, s.bs_row0, s.bs_n,
+                                                                 s.bs_len0, device_error_flag());
+    return launch_check("verify_setup");
+}
+
+// ---------------------------------------------------------------------------
+// Acceptance (src/engine.cpp:333-365 with D7): accept drafts while the main
+// model's greedy token of the previous row equals the draft; the row after
+// the accepted prefix gives the next token.
+// ---------------------------------------------------------------------------
+__global__ void accept_kernel(int n_seqs, int K, const int* __restrict__ amax, const int* __restrict__ drafts,
+                              const int* __restrict__ bs_n, int* __restrict__ n_commit, int* __restrict__ final_row) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= n_seqs) return;
+    const int R = K + 1;
+    if (bs_n[b] == 0) {
+        n_commit[b] = 0;
+        final_row[b] = b * R;
+        return;
+    }
+    int a = 0;
+    while (a < K && amax[b * R + a] == drafts[b * K + a]) a++;
+    n_commit[b] = a + 1;
+    final_row[b] = b * R + a;
+}
+
+pf_status accept(const StepBufs& s, cudaStream_t st) {
+    accept_kernel<<<ceil_div(s.n_seqs, 128), 128, 0, st>>>(s.n_seqs, s.K, s.amax, s.drafts, s.bs_n, s.n_commit,
+                                                           s.final_row);
+    return launch_check("accept");
+}
+
+// ---------------------------------------------------------------------------
+// Finish: emitted tokens, pending token, lengths, token log.
+// ---------------------------------------------------------------------------
+__global__ void finish_kernel(int n_seqs, int K, const int* __restrict__ next, const int* __restrict__ n_commit,
+                              const int* __restrict__ drafts, int* __restrict__ pending, int* __restrict__ seq_len,
+                              int* __restrict__ emitted, int* __restrict__ n_emitted, int* __restrict__ log,
+                              int log_cap, int* __restrict__ n_logged) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= n_seqs) return;
+    const int R = K + 1;
+    const int nc = n_commit[b];
+    n_emitted[b] = nc;
+    for (int j = 0; j < R; j++) {
+        int t = -1;
+        if (nc > 0) t = (j < nc - 1) ? drafts[b * K + j] : (j == nc - 1 ? next[b] : -1);
+        emitted[b * R + j] = t;
+    }
+    if (nc == 0) return;
+    pending[b] = next[b];
+    seq_len[b] += nc;
+    if (log) {
+        int c = n_logged[b];
+        for (int j = 0; j < nc && c < log_cap; j++, c++) log[(size_t)b * log_cap + c] = emitted[b * R + j];
+        n_logged[b] = c;
+    }
+}
+
+pf_status finish(const StepBufs& s, const int* next, cudaStream_t st) {
+    finish_kernel<<<ceil_div(s.n_seqs, 128), 128, 0, st>>>(s.n_seqs, s.K, next, s.n_commit, s.drafts, s.pending,
+                                                           s.seq_len, s.emitted, s.n_emitted, s.log, s.log_cap,
+                                                           s.n_logged);
+    return launch_check("finish");
+}
+
+// Copies row idx[b] of x[.][d] to out[b][d].
+__global__ void gather_rows_kernel(const float* __restrict__ x, int d, const int* __restrict__ idx, int n,
+                                   float* __restrict__ out) {
+    const int b = blockIdx.x;
+    if (b >= n) return;
+    const float* src = x + (size_t)idx[b] * d;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) out[(size_t)b * d + i] = src[i];
+}
+
+pf_status gather_rows(const float* x, int d, const int* idx, int n, float* out, cudaStream_t st) {
+    gather_rows_kernel<<<n, 256, 0, st>>>(x, d, idx, n, out);
+    return launch_check("gather_rows");
+}
+
+// ---------------------------------------------------------------------------
+// Stochastic sampling of one row per sequence (src/engine.cpp:881-1003).
+// Dispatch as the reference: top-p when 0<p<1 (top-k is then ignored),
+// else top-k when 0<k<V, else plain temperature.  One CTA sorts the row
+// (descending value, ascending index on ties) with a bitonic sort in shared
+// memory; cumulative sums run in double, so a draw can differ from the
+// reference's float sums only when it lands within float rounding of a
+// cumulative boundary.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int SORT_THREADS = 1024;
+
+__device__ __forceinline__ bool before(float va, int ia, float vb, int ib) {
+    return va > vb || (va == vb && ia < ib);
+}
+
+// Inclusive block scan of one double per thread.
+__device__ double block_scan(double v, double* sh) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    for (int o = 1; o < 32; o <<= 1) {
+        const double t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+    }
+    if (lane == 31) sh[w] = v;
+    __syncthreads();
+    if (w == 0) {
+        double t = (lane < (blockDim.x >> 5)) ? sh[lane] : 0.0;
+        for (int o = 1; o < 32; o <<= 1) {
+            const double u = __shfl_up_sync(0xffffffffu, t, o);
+            if (lane >= o) t += u;
+        }
+        sh[lane] = t;
+    }
+    __syncthreads();
+    const double base = (w > 0) ? sh[w - 1] : 0.0;
+    __syncthreads();
+    return v + base;
+}
+}  // namespace
+
+__global__ void __launch_bounds__(SORT_THREADS) sample_kernel(const float* __restrict__ logits, int ld, int V, int P2,
+                                                              const int* __restrict__ rows, int n, pf_sampling_config cfg,
+                                                              const float* __restrict__ uniforms, int ustride,
+                                                              int* __restrict__ out) {
+    extern __shared__ __align__(16) uint8_t sm[];
+    float* key = reinterpret_cast<float*>(sm);
+    int* idx = reinterpret_cast<int*>(sm + (size_t)P2 * sizeof(float));
+    __shared__ double sh[32];
+    const int b = blockIdx.x;
+    if (b >= n) return;
+    const float* lg = logits + (size_t)rows[b] * ld;
+    const float u = uniforms[(size_t)b * ustride];
+    const float t = fmaxf(cfg.temperature, 0.001f);
+    const bool top_p = cfg.top_p < 1.0f && cfg.top_p > 0.0f;
+    const bool top_k = !top_p && cfg.top_k > 0 && (int)cfg.top_k < V;
+    const int tid = threadIdx.x;
+    if (!top_p && !top_k) {
+        // temperature sampling over index order
+        float mx = -INFINITY;
+        for (int i = tid; i < V; i += blockDim.x) mx = fmaxf(mx, lg[i]);
+        for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if ((tid & 31) == 0) sh[tid >> 5] = mx;
+        __syncthreads();
+        mx = -INFINITY;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) mx = fmaxf(mx, (float)sh[w]);
+        __syncthreads();
+        const int per = ceil_div(V, blockDim.x);
+        double loc = 0.0;
+        for (int j = 0; j < per; j++) {
+            const int i = tid * per + j;
+            if (i < V) loc += (double)expf((lg[i] - mx) / t);
+        }
+        const double incl = block_scan(loc, sh);
+        const double total = sh[(blockDim.x >> 5) - 1];
+        double c;
+        // first thread-local hit in index order
+        __shared__ int s_first;
+        if (tid == 0) s_first = 0x7fffffff;
+        __syncthreads();
+        c = incl - loc;
+        for (int j = 0; j < per; j++) {
+            const int i = tid * per + j;
+            if (i >= V) break;
+            c += (double)expf((lg[i] - mx) / t);
+            if ((double)u <= c / total) {
+                atomicMin(&s_first, i);
+                break;
+            }
+        }
+        __syncthreads();
+        if (tid == 0) out[b] = (s_first == 0x7fffffff) ? V - 1 : s_first;
+        return;
+    }
+    for (int i = tid; i < P2; i += blockDim.x) {
+        key[i] = i < V ? lg[i] : -INFINITY;
+        idx[i] = i < V ? i : 0x7fffffff;
+    }
+    __syncthreads();
+    for (int k = 2; k <= P2; k <<= 1)
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = tid; i < P2; i += blockDim.x) {
+                const int p = i ^ j;
+                if (p > i) {
+                    const bool up = (i & k) == 0;  // "up" segments sort descending
+                    const bool swap = up ? before(key[p], idx[p], key[i], idx[i]) : before(key[i], idx[i], key[p], idx[p]);
+                    if (swap) {
+                        const float tk = key[i];
+                        key[i] = key[p];
+                        key[p] = tk;
+                        const int ti = idx[i];
+                        idx[i] = idx[p];
+                        idx[p] = ti;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    const float mx = key[0];
+    const int nn = top_p ? V : (int)cfg.top_k;
+    const int per = ceil_div(nn, blockDim.x);
+    double loc = 0.0;
+    for (int j = 0; j < per; j++) {
+        const int i = tid * per + j;
+        if (i < nn) loc += (double)expf((key[i] - mx) / t);
+    }
+    const double incl = block_scan(loc, sh);
+    const double total = sh[(blockDim.x >> 5) - 1];
+    __shared__ int s_cut, s_pick;
+    if (tid == 0) {
+        s_cut = nn;
+        s_pick = 0x7fffffff;
+    }
+    __syncthreads();
+    if (top_p) {
+        double c = incl - loc;
+        for (int j = 0; j < per; j++) {
+            const int i = tid * per + j;
+            if (i >= nn) break;
+            c += (double)expf((key[i] - mx) / t);
+            if (c / total >= (double)cfg.top_p) {
+                atomicMin(&s_cut, i + 1);
+                break;
+            }
+        }
+        __syncthreads();
+    }
+    const int cut = s_cut;
+    {
+        double c = incl - loc;
+        for (int j = 0; j < per; j++) {
+            const int i = tid * per + j;
+            if (i >= cut) break;
+            c += (double)expf((key[i] - mx) / t);
+            if ((double)u <= c / total) {
+                atomicMin(&s_pick, i);
+                break;
+            }
+        }
+    }
+    __syncthreads();
+    if (tid == 0) out[b] = idx[(s_pick == 0x7fffffff) ? cut - 1 : s_pick];
+}
+
+pf_status sample_rows(const float* logits, int ld, int V, const int* rows, int n, const pf_sampling_config& cfg,
+                      const float* uniforms, int ustride, int* out, cudaStream_t st) {
+    int P2 = 1;
+    while (P2 < V) P2 <<= 1;
+    PF_CHECK(P2 <= 16384, "sample_rows: vocabulary above 16384 is not supported");
+    const size_t smem = (size_t)P2 * (sizeof(float) + sizeof(int));
+    static bool attr = false;
+    if (!attr) {
+        PF_CUDA(cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 16384 * 8));
+        attr = true;
+    }
+    sample_kernel<<<n, SORT_THREADS, smem, st>>>(logits, ld, V, P2, rows, n, cfg, uniforms, ustride, out);
+    return launch_check("sample_rows");
+}
+
+// Copies idx-selected int values: out[b] = src[idx[b]].
+__global__ void pick_kernel(const int* __restrict__ src, const int* __restrict__ idx, int n, int* __restrict__ out) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < n) out[b] = src[idx[b]];
+}
+pf_status pick(const int* src, const int* idx, int n, int* out, cudaStream_t st) {
+    pick_kernel<<<ceil_div(n, 128), 128, 0, st>>>(src, idx, n, out);
+    return launch_check("pick");
+}
+
+// Writes draft h of every sequence: drafts[b*K + h] = tok[b].
+__global__ void put_draft_kernel(const int* __restrict__ tok, int n, int K, int h, int* __restrict__ drafts) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < n) drafts[b * K + h] = tok[b];
+}
+pf_status put_draft(const int* tok, int n, int K, int h, int* drafts, cudaStream_t st) {
+    put_draft_kernel<<<ceil_div(n, 128), 128, 0, st>>>(tok, n, K, h, drafts);
+    return launch_check("put_draft");
+}
+
+// ---------------------------------------------------------------------------
+// Predictive FFN skip (LayerSkipController::should_skip_ffn,
+// src/layer_skip.cpp:22-67): rows of a sequence in order, each compared with
+// the post-norm vector of the last row whose FFN ran (committed cache at the
+// start).  One warp per sequence; the RMS delta uses the device sum order.
+// ---------------------------------------------------------------------------
+__global__ void skip_decide_kernel(int nb, const int* __restrict__ bs_row0, const int* __restrict__ bs_n,
+                                   const float* __restrict__ normed, int d, const float* __restrict__ cache,
+                                   size_t cache_stride, float thr_l, uint8_t* __restrict__ skip) {
+    const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (b >= nb) return;
+    const int n = bs_n[b], row0 = bs_row0[b];
+    const float* ref = cache + (size_t)b * cache_stride;
+    for (int r = 0; r < n; r++) {
+        const float* x = normed + (size_t)(row0 + r) * d;
+        float s = 0.0f;
+        for (int i = lane; i < d; i += 32) {
+            const float df = __fsub_rn(x[i], ref[i]);
+            s = __fadd_rn(s, __fmul_rn(df, df));
+        }
+        for (int o = 16; o >= 1; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+        const float delta = __fsqrt_rn(__fdiv_rn(s, (float)d));
+        const bool sk = delta < thr_l;
+        if (lane == 0) skip[row0 + r] = sk ? 1 : 0;
+        if (!sk) ref = x;
+    }
+}
+
+pf_status skip_decide(int nb, const int* bs_row0, const int* bs_n, const float* normed, int d, const float* cache,
+                      size_t cache_stride, float thr_l, uint8_t* skip, cudaStream_t st) {
+    skip_decide_kernel<<<ceil_div(nb, 4), 128, 0, st>>>(nb, bs_row0, bs_n, normed, d, cache, cache_stride, thr_l,
+                                                        skip);
+    return launch_check("skip_decide");
+}
+
+// After acceptance: the skip cache of layer l becomes the post-norm vector of
+// the last committed row whose FFN ran at that layer (unchanged if none).
+__global__ void skip_commit_kernel(int nb, int L, int d, int Mst, const int* __restrict__ bs_row0,
+                                   const int* __restrict__ n_commit, const uint8_t* __restrict__ skip_all,
+                                   const float* __restrict__ normed_all, float* __restrict__ cache,
+                                   long long* __restrict__ counts) {
+    const int b = blockIdx.x, l = blockIdx.y;
+    const int nc = n_commit[b];
+    if (nc <= 0) return;
+    const int row0 = bs_row0[b];
+    const uint8_t* sk = skip_all + (size_t)l * Mst;
+    int last = -1, ns = 0;
+    for (int r = 0; r < nc; r++) {
+        if (!sk[row0 + r]) last = r;
+        else ns++;
+    }
+    if (threadIdx.x == 0) {
+        atomicAdd(reinterpret_cast<unsigned long long*>(counts + 0), (unsigned long long)(nc - ns));
+        atomicAdd(reinterpret_cast<unsigned long long*>(counts + 1), (unsigned long long)ns);
+    }
+    if (last < 0) return;
+    const float* src = normed_all + ((size_t)l * Mst + row0 + last) * d;
+    float* dst = cache + ((size_t)b * L + l) * d;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) dst[i] = src[i];
+}
+
+pf_status skip_commit(int nb, int L, int d, int Mst, const int* bs_row0, const int* n_commit, const uint8_t* skip_all,
+                      const float* normed_all, float* cache, long long* counts, cudaStream_t st) {
+    dim3 grid(nb, L);
+    skip_commit_kernel<<<grid, 256, 0, st>>>(nb, L, d, Mst, bs_row0, n_commit, skip_all, normed_all, cache, counts);
+    return launch_check("skip_commit");
+}
+
+// Counts rows whose FFN ran / was skipped when no skip cache is kept.
+__global__ void ffn_count_kernel(int nb, int L, const int* __restrict__ n_commit, long long* __restrict__ counts) {
+    long long tot = 0;
+    for (int b = threadIdx.x; b < nb; b += blockDim.x) tot += max(0, n_commit[b]);
+    for (int o = 16; o >= 1; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+    if ((threadIdx.x & 31) == 0) atomicAdd(reinterpret_cast<unsigned long long*>(counts), (unsigned long long)(tot * L));
+}
+pf_status ffn_count(int nb, int L, const int* n_commit, long long* counts, cudaStream_t st) {
+    ffn_count_kernel<<<1, 32, 0, st>>>(nb, L, n_commit, counts);
+    return launch_check("ffn_count");
+}
+
+}  // namespace pf

@@ -1,0 +1,280 @@
+// rows.cu — row-wise kernels of the decode step: RMSNorm + int8 quantization,
+// activation quantization, the 3-digit split of fp32 rows for the exact-int
+// tensor-core unembed, embedding gather, argmax, softmax.
+//
+// One warp per row.  RMSNorm's sum of squares uses a fixed order ("device
+// order"): lane l sums elements l, l+32, ... sequentially, then an xor
+// butterfly over offsets 16..1; oracle/pf_oracle.cpp restates the same order
+// (order=1) so the GPU result can be checked bit for bit, and the reference's
+// sequential order (order=0) within tolerance.
+#include "common.cuh"
+#include "rows.cuh"
+
+namespace pf {
+
+__device__ __forceinline__ float warp_sum_xor(float v) {
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// quantize_activation_row (src/matmul_neon.cpp:16-29) of a row already in
+// registers / memory: amax, mul = 127/amax, q = round(x*mul), scale = amax/127.
+__device__ __forceinline__ void row_quant_params(float amax, float& mul, float& scale) {
+    mul = (amax == 0.0f) ? 1.0f : __fdiv_rn(127.0f, amax);
+    scale = (amax == 0.0f) ? 1.0f : __fdiv_rn(amax, 127.0f);
+}
+__device__ __forceinline__ int8_t q8(float x, float mul) { return (int8_t)(int)roundf(__fmul_rn(x, mul)); }
+
+// ---------------------------------------------------------------------------
+// RMSNorm (src/matmul_neon.cpp:231-239) fused with the activation quantizer.
+// normed (optional) receives the fp32 output; q/qs the int8 row and scale.
+// ---------------------------------------------------------------------------
+__global__ void rmsnorm_quant_kernel(const float* __restrict__ x, const float* __restrict__ w, int n,
+                                     float eps, int M, const int* m_dev, float* __restrict__ normed,
+                                     int8_t* __restrict__ q, float* __restrict__ qs, int ldq) {
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    const int m_act = m_dev ? min(M, *m_dev) : M;
+    if (row >= m_act) return;
+    const float* xr = x + (size_t)row * n;
+    float ss = 0.0f;
+    for (int i = lane; i < n; i += 32) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
+    ss = warp_sum_xor(ss);
+    const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps));
+    const float inv = __fdiv_rn(1.0f, rms);
+    float amax = 0.0f;
+    for (int i = lane; i < n; i += 32) {
+        const float v = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+        if (normed) normed[(size_t)row * n + i] = v;
+        amax = fmaxf(amax, fabsf(v));
+    }
+    amax = warp_max(amax);
+    if (!q) return;
+    float mul, scale;
+    row_quant_params(amax, mul, scale);
+    for (int i = lane; i < n; i += 32) {
+        const float v = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+        q[(size_t)row * ldq + i] = q8(v, mul);
+    }
+    if (lane == 0) qs[row] = scale;
+}
+
+pf_status rmsnorm_quant(const float* x, const float* w, int n, float eps, int M, const int* m_dev,
+                        float* normed, int8_t* q, float* qs, int ldq, cudaStream_t st) {
+    const int rows_per_block = 4;
+    rmsnorm_quant_kernel<<<ceil_div(M, rows_per_block), 32 * rows_per_block, 0, st>>>(
+        x, w, n, eps, M, m_dev, normed, q, qs, ldq);
+    return launch_check("rmsnorm_quant");
+}
+
+// ---------------------------------------------------------------------------
+// quantize_activation_row over M rows.
+// ---------------------------------------------------------------------------
+__global__ void quant_rows_kernel(const float* __restrict__ x, int n, int ldx, int M, const int* m_dev,
+                                  int8_t* __restrict__ q, float* __restrict__ qs, int ldq) {
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    const int m_act = m_dev ? min(M, *m_dev) : M;
+    if (row >= m_act) return;
+    const float* xr = x + (size_t)row * ldx;
+    float amax = 0.0f;
+    for (int i = lane; i < n; i += 32) amax = fmaxf(amax, fabsf(xr[i]));
+    amax = warp_max(amax);
+    float mul, scale;
+    row_quant_params(amax, mul, scale);
+    int8_t* qr = q + (size_t)row * ldq;
+    for (int i = lane; i < n; i += 32) qr[i] = q8(xr[i], mul);
+    if (lane == 0) qs[row] = scale;
+}
+
+pf_status quant_rows(const float* x, int n, int ldx, int M, const int* m_dev, int8_t* q, float* qs, int ldq,
+                     cudaStream_t st) {
+    quant_rows_kernel<<<ceil_div(M, 4), 128, 0, st>>>(x, n, ldx, M, m_dev, q, qs, ldq);
+    return launch_check("quant_rows");
+}
+
+// Rows quantized with caller-given scales: q = round(x / s) (the act_scales
+// branch of matmul_quantized, src/matmul_neon.cpp:158-164).
+__global__ void quant_rows_given_kernel(const float* __restrict__ x, int n, int M, const float* __restrict__ s,
+                                        int8_t* __restrict__ q, float* __restrict__ qs, int ldq) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)M * n) return;
+    const int row = (int)(i / n), col = (int)(i % n);
+    q[(size_t)row * ldq + col] = (int8_t)(int)roundf(__fdiv_rn(x[i], s[row]));
+    if (col == 0) qs[row] = s[row];
+}
+
+pf_status quant_rows_given(const float* x, int n, int M, const float* s, int8_t* q, float* qs, int ldq,
+                           cudaStream_t st) {
+    const int64_t tot = (int64_t)M * n;
+    quant_rows_given_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, st>>>(x, n, M, s, q, qs, ldq);
+    return launch_check("quant_rows_given");
+}
+
+// ---------------------------------------------------------------------------
+// Three int8 digit planes of an fp32 row: with s = amax/127 and r0 = x*127/amax,
+// q1 = rint(r0), q2 = rint((r0-q1)*254), q3 = rint(((r0-q1)*254-q2)*254), so
+// x ~= s*(q1 + q2/254 + q3/254^2) to ~2^-23 of amax.  Integer MMAs over the
+// planes then reproduce an fp32 dot product to ~1e-7 relative.
+// ---------------------------------------------------------------------------
+__global__ void split_digits_kernel(const float* __restrict__ x, int n, int ldx, int M, const int* m_dev,
+                                    int8_t* __restrict__ q, int64_t plane, int ldq, float* __restrict__ qs) {
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    const int m_act = m_dev ? min(M, *m_dev) : M;
+    if (row >= m_act) return;
+    const float* xr = x + (size_t)row * ldx;
+    float amax = 0.0f;
+    for (int i = lane; i < n; i += 32) amax = fmaxf(amax, fabsf(xr[i]));
+    amax = warp_max(amax);
+    const float mul = (amax == 0.0f) ? 0.0f : __fdiv_rn(127.0f, amax);
+    for (int i = lane; i < n; i += 32) {
+        const float r0 = __fmul_rn(xr[i], mul);
+        const float d1 = rintf(r0);
+        const float r1 = __fmul_rn(__fsub_rn(r0, d1), 254.0f);
+        const float d2 = rintf(r1);
+        const float r2 = __fmul_rn(__fsub_rn(r1, d2), 254.0f);
+        const float d3 = fminf(127.0f, fmaxf(-127.0f, rintf(r2)));
+        const size_t o = (size_t)row * ldq + i;
+        q[o] = (int8_t)(int)d1;
+        q[o + plane] = (int8_t)(int)d2;
+        q[o + 2 * plane] = (int8_t)(int)d3;
+    }
+    if (lane == 0) qs[row] = (amax == 0.0f) ? 1.0f : __fdiv_rn(amax, 127.0f);
+}
+
+pf_status split_digits(const float* x, int n, int ldx, int M, const int* m_dev, int8_t* q, int64_t plane,
+                       int ldq, float* qs, cudaStream_t st) {
+    split_digits_kernel<<<ceil_div(M, 4), 128, 0, st>>>(x, n, ldx, M, m_dev, q, plane, ldq, qs);
+    return launch_check("split_digits");
+}
+
+// ---------------------------------------------------------------------------
+// Tied embedding gather (src/engine.cpp:476-484): x = E[token] * global_scale,
+// zeros for ids outside [0, n_vocab).
+// ---------------------------------------------------------------------------
+__global__ void embed_kernel(const int8_t* __restrict__ emb, float gscale, int d, int V, const int* __restrict__ tok,
+                             int M, const int* m_dev, float* __restrict__ x) {
+    const int row = blockIdx.x;
+    const int m_act = m_dev ? min(M, *m_dev) : M;
+    if (row >= m_act) return;
+    const int t = tok[row];
+    const bool ok = t >= 0 && t < V;
+    for (int i = threadIdx.x; i < d; i += blockDim.x)
+        x[(size_t)row * d + i] = ok ? __fmul_rn((float)emb[(size_t)t * d + i], gscale) : 0.0f;
+}
+
+pf_status embed(const int8_t* emb, float gscale, int d, int V, const int* tok, int M, const int* m_dev, float* x,
+                cudaStream_t st) {
+    embed_kernel<<<M, 256, 0, st>>>(emb, gscale, d, V, tok, M, m_dev, x);
+    return launch_check("embed");
+}
+
+// ---------------------------------------------------------------------------
+// argmax with the first-maximum rule (strict >, src/engine.cpp:918-928).
+// ---------------------------------------------------------------------------
+__global__ void argmax_kernel(const float* __restrict__ v, int n, int ld, int M, const int* m_dev,
+                              int* __restrict__ out) {
+    const int row = blockIdx.x;
+    const int m_act = m_dev ? min(M, *m_dev) : M;
+    if (row >= m_act) return;
+    const float* r = v + (size_t)row * ld;
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float x = r[i];
+        if (x > best) {  // strided scan: earlier index wins ties within a thread
+            best = x;
+            bi = i;
+        }
+    }
+    for (int o = 16; o >= 1; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ob > best || (ob == best && oi < bi)) {
+            best = ob;
+            bi = oi;
+        }
+    }
+    __shared__ float sb[32];
+    __shared__ int si[32];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        sb[w] = best;
+        si[w] = bi;
+    }
+    __syncthreads();
+    if (w == 0) {
+        const int nw = blockDim.x >> 5;
+        best = lane < nw ? sb[lane] : -INFINITY;
+        bi = lane < nw ? si[lane] : 0x7fffffff;
+        for (int o = 16; o >= 1; o >>= 1) {
+            const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ob > best || (ob == best && oi < bi)) {
+                best = ob;
+                bi = oi;
+            }
+        }
+        // All -inf / NaN rows: the reference returns index 0.
+        if (lane == 0) out[row] = (bi == 0x7fffffff) ? 0 : bi;
+    }
+}
+
+pf_status argmax_rows(const float* v, int n, int ld, int M, const int* m_dev, int* out, cudaStream_t st) {
+    argmax_kernel<<<M, 256, 0, st>>>(v, n, ld, M, m_dev, out);
+    return launch_check("argmax");
+}
+
+// ---------------------------------------------------------------------------
+// Reference-interface helpers (kernel-level C ABI only).
+// ---------------------------------------------------------------------------
+__global__ void rmsnorm_rows_kernel(float* __restrict__ out, const float* __restrict__ x, const float* __restrict__ w,
+                                    int M, int n) {
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= M) return;
+    const float* xr = x + (size_t)row * n;
+    float ss = 0.0f;
+    for (int i = lane; i < n; i += 32) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
+    ss = warp_sum_xor(ss);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), 1e-6f)));
+    for (int i = lane; i < n; i += 32) out[(size_t)row * n + i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+}
+
+pf_status rmsnorm_rows(float* out, const float* x, const float* w, int M, int n, cudaStream_t st) {
+    rmsnorm_rows_kernel<<<ceil_div(M, 4), 128, 0, st>>>(out, x, w, M, n);
+    return launch_check("rmsnorm_rows");
+}
+
+__global__ void softmax_rows_kernel(float* __restrict__ v, int M, int n) {
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= M) return;
+    float* r = v + (size_t)row * n;
+    float mx = -INFINITY;
+    for (int i = lane; i < n; i += 32) mx = fmaxf(mx, r[i]);
+    mx = warp_max(mx);
+    float s = 0.0f;
+    for (int i = lane; i < n; i += 32) {
+        const float e = expf(__fsub_rn(r[i], mx));
+        r[i] = e;
+        s = __fadd_rn(s, e);
+    }
+    s = warp_sum_xor(s);
+    const float inv = __fdiv_rn(1.0f, __fadd_rn(s, 1e-10f));
+    for (int i = lane; i < n; i += 32) r[i] = __fmul_rn(r[i], inv);
+}
+
+pf_status softmax_rows(float* v, int M, int n, cudaStream_t st) {
+    softmax_rows_kernel<<<ceil_div(M, 4), 128, 0, st>>>(v, M, n);
+    return launch_check("softmax_rows");
+}
+
+}  // namespace pf

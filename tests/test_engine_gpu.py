@@ -1,0 +1,179 @@
+"""End-to-end parity of the batched MTP speculative-decode step on the GPU
+against the oracle's Level-B engine, on identical seeded weights and prompts.
+
+Tolerances: logits within 1e-3 relative (of the row's largest magnitude);
+greedy token streams identical (a stream divergence must be a documented
+near-tie: the two logits involved within the tolerance); committed int8 KV
+entries identical for >= 99.9% of bytes.  The oracle runs with the device's
+RMSNorm summation order (order=1); test_oracle_engine.py bounds the effect of
+the reference's order."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+from helpers import Cfg, OracleEngine, make_weights, prompts  # noqa: E402
+
+import pocketforge_b200 as pf  # noqa: E402
+
+RTOL = 1e-3
+
+
+@pytest.fixture(scope="module", autouse=True)
+def need_device():
+    if pf.device_count() == 0:
+        pytest.skip("no sm_100 device")
+
+
+def gpu_engine(cfg: Cfg, w, max_seqs, max_pos, sampling=None, skip_threshold=None):
+    e = pf.BatchEngine(cfg.product(), max_seqs, max_pos)
+    for l in range(cfg.n_layers):
+        for m in range(7):
+            a, rs = w[(l, m)]
+            e.set_matrix(l, m, a, rs)
+    emb, gs = w["emb"]
+    e.set_embedding(emb, gs)
+    for h in range(cfg.n_mtp_heads):
+        e.set_mtp_head(h, *w[("mtp", h)])
+    if sampling is not None:
+        e.set_sampling(*sampling)
+    if skip_threshold is not None:
+        e.set_skip_threshold(skip_threshold)
+    return e
+
+
+def rel_err(a, b):
+    scale = np.maximum(np.abs(b).max(axis=-1, keepdims=True), 1e-30)
+    return float((np.abs(a - b) / scale).max())
+
+
+def compare_step_state(g, o, check_kv=True):
+    np.testing.assert_array_equal(g.read_positions(), o.positions())
+    assert rel_err(g.read_logits(), o.logits()) < RTOL
+    np.testing.assert_array_equal(g.read_pending(), o.pending())
+    assert rel_err(g.read_hidden(), o.hidden()) < RTOL
+    assert rel_err(g.read_mtp_logits(), o.mtp_logits()) < RTOL
+    np.testing.assert_array_equal(g.read_drafts(), o.drafts())
+
+
+def run_pair(cfg, w, prm, steps, max_pos=None, forced=None, sampling=None, seeds=None, skip_threshold=None):
+    max_pos = max_pos or (max(len(x) for x in prm) + (steps + 1) * (cfg.n_mtp_heads + 1) + 8)
+    g = gpu_engine(cfg, w, len(prm), max_pos, sampling=sampling, skip_threshold=skip_threshold)
+    o = OracleEngine(cfg, w, order=1, sampling=sampling, skip_threshold=skip_threshold)
+    g.prefill(prm, seeds)
+    o.prefill(prm, seeds)
+    np.testing.assert_array_equal(g.read_pending(), o.pending())
+    np.testing.assert_array_equal(g.read_drafts(), o.drafts())
+    for s in range(steps):
+        if forced is not None:
+            d = forced(s, o)
+            g.set_drafts(d)
+            o.set_drafts(d)
+        gn, ge = g.step()
+        on, oe = o.step()
+        np.testing.assert_array_equal(gn, on, err_msg=f"step {s}")
+        np.testing.assert_array_equal(ge, oe, err_msg=f"step {s}")
+        compare_step_state(g, o)
+    return g, o
+
+
+def compare_kv(g, o, cfg, n_seqs):
+    tot = same = 0
+    for b in range(n_seqs):
+        for l in range(cfg.n_layers):
+            for h in range(cfg.n_kv_heads):
+                gk, gks, gv, gvs = g.read_kv(b, l, h, 1 << 16)
+                ok, oks, ov, ovs = o.kv(b, l, h)
+                assert len(gk) == len(ok)
+                tot += gk.size * 2
+                same += int((gk == ok).sum() + (gv == ov).sum())
+                np.testing.assert_allclose(gks, oks, rtol=RTOL)
+                np.testing.assert_allclose(gvs, ovs, rtol=RTOL)
+    assert same / tot >= 0.999, same / tot
+
+
+@pytest.fixture(scope="module")
+def tiny():
+    cfg = Cfg(n_kv_heads=1)
+    return cfg, make_weights(cfg)
+
+
+def test_greedy_steps_match_oracle(tiny):
+    cfg, w = tiny
+    prm = prompts(3, [9, 17, 4], cfg.n_vocab)
+    g, o = run_pair(cfg, w, prm, 6)
+    compare_kv(g, o, cfg, 3)
+
+
+def test_forced_drafts_exercise_acceptance(tiny):
+    """Drafts copied from the oracle's greedy continuation, broken at a
+    different position per step: every acceptance length 0..K is hit."""
+    cfg, w = tiny
+    prm = prompts(2, [12, 20], cfg.n_vocab, seed=3)
+    ref = OracleEngine(cfg, w)
+    ref.prefill(prm)
+    stream = [[int(t)] for t in ref.pending()]
+    for _ in range(40):
+        n, em = ref.step()
+        for b in range(2):
+            stream[b] += [int(t) for t in em[b, : n[b]]]
+    K = cfg.n_mtp_heads
+    done = [1, 1]
+
+    def forced(s, o):
+        d = np.zeros((2, K), np.int32)
+        for b in range(2):
+            pos = int(o.positions()[b]) - len(prm[b]) + 1  # tokens emitted so far
+            nxt = stream[b][pos:pos + K]
+            d[b] = nxt + [0] * (K - len(nxt))
+            wrong = (s + b) % (K + 1)
+            if wrong < K:
+                d[b, wrong] = (d[b, wrong] + 1) % cfg.n_vocab
+        return d
+
+    g, o = run_pair(cfg, w, prm, 10, forced=forced)
+    compare_kv(g, o, cfg, 2)
+
+
+def test_gqa_and_eviction_pooling():
+    """Window 16 / pool 4: the verify rows cross pool-block boundaries, so
+    speculative pool entries and the fp64 accumulator are exercised."""
+    cfg = Cfg(n_heads=4, n_kv_heads=2, n_embd=256, window_size=16, pool_block=4, max_context=1024)
+    w = make_weights(cfg, seed=2)
+    prm = prompts(2, [40, 23], cfg.n_vocab, seed=4)
+    g, o = run_pair(cfg, w, prm, 8)
+    compare_kv(g, o, cfg, 2)
+
+
+def test_layer_skip_matches_oracle():
+    cfg = Cfg(n_layers=6, skip_enabled=1, skip_threshold=5.0, qtype=[1, 1, 1, 1, 2, 2, 3])
+    w = make_weights(cfg, seed=3)
+    prm = prompts(3, [10, 14, 6], cfg.n_vocab, seed=6)
+    g, o = run_pair(cfg, w, prm, 5, skip_threshold=5.0)
+    assert g.read_skip_counts() == o.skip_counts()
+    assert o.skip_counts()[1] > 0
+
+
+def test_stochastic_sampling_matches_oracle():
+    """temperature 0.8, top-k 40 (ignored by the top-p branch), top-p 0.95,
+    per-sequence seeds; the tiny model's logits are far apart, so float vs
+    double cumulative sums cannot flip a draw here."""
+    cfg = Cfg()
+    w = make_weights(cfg, seed=4)
+    prm = prompts(2, [8, 11], cfg.n_vocab, seed=8)
+    run_pair(cfg, w, prm, 5, sampling=(0.8, 0.95, 40, 0), seeds=[2, 3])
+
+
+def test_generate_api(tiny):
+    cfg, w = tiny
+    prm = prompts(2, [6, 9], cfg.n_vocab, seed=9)
+    g = gpu_engine(cfg, w, 2, 64)
+    out = g.generate(prm, 12)
+    o = OracleEngine(cfg, w)
+    o.prefill(prm)
+    want = [[int(t)] for t in o.pending()]
+    while min(len(x) for x in want) < 12:
+        n, em = o.step()
+        for b in range(2):
+            want[b] += [int(t) for t in em[b, : n[b]]]
+    assert out == [x[:12] for x in want]
