@@ -251,7 +251,9 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
+        torch.cuda.nvtx.range_push("pf_timed")  # ncu --nvtx-include pf_timed/ selects these launches
         ms = eng.run_steps(args.steps)
+        torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     pos1 = eng.read_positions().astype(np.int64)
     tokens = int((pos1 - pos0).sum())

@@ -120,23 +120,30 @@ static void mm_quant(const float* A, const int8_t* B, float* C, uint32_t M, uint
 // ---------------------------------------------------------------------------
 // A5: rmsnorm (src/matmul_neon.cpp:231-239).
 // order 0: the reference's sequential sum of squares.
-// order 1: the device order — 32 lanes, lane l sums elements l, l+32, ...
-//          in sequence, then an xor butterfly over offsets 16,8,4,2,1
-//          (every lane ends with the same value; lane 0's is taken).
+// order 1: the device order — 256 threads, thread t sums elements t, t+256,
+//          ... in sequence; each warp of 32 threads combines with an xor
+//          butterfly over offsets 16,8,4,2,1 (every lane ends with the same
+//          value); the 8 warp totals are added in warp order.
 // ---------------------------------------------------------------------------
 static float sumsq_lanes(const float* x, uint32_t n) {
-    float s[32];
-    for (int l = 0; l < 32; l++) {
-        float a = 0.0f;
-        for (uint32_t i = (uint32_t)l; i < n; i += 32) a += x[i] * x[i];
-        s[l] = a;
+    float warp_total[8];
+    for (int w = 0; w < 8; w++) {
+        float s[32];
+        for (int l = 0; l < 32; l++) {
+            float a = 0.0f;
+            for (uint32_t i = (uint32_t)(w * 32 + l); i < n; i += 256) a += x[i] * x[i];
+            s[l] = a;
+        }
+        for (int off = 16; off >= 1; off >>= 1) {
+            float t[32];
+            for (int l = 0; l < 32; l++) t[l] = s[l] + s[l ^ off];
+            std::memcpy(s, t, sizeof(s));
+        }
+        warp_total[w] = s[0];
     }
-    for (int off = 16; off >= 1; off >>= 1) {
-        float t[32];
-        for (int l = 0; l < 32; l++) t[l] = s[l] + s[l ^ off];
-        std::memcpy(s, t, sizeof(s));
-    }
-    return s[0];
+    float tot = warp_total[0];
+    for (int w = 1; w < 8; w++) tot += warp_total[w];
+    return tot;
 }
 
 static float sumsq(const float* x, uint32_t n, int order) {

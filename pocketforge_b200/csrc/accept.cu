@@ -116,10 +116,14 @@ pf_status gather_rows(const float* x, int d, const int* idx, int n, float* out, 
 // Stochastic sampling of one row per sequence (src/engine.cpp:881-1003).
 // Dispatch as the reference: top-p when 0<p<1 (top-k is then ignored),
 // else top-k when 0<k<V, else plain temperature.  One CTA sorts the row
-// (descending value, ascending index on ties) with a bitonic sort in shared
-// memory; cumulative sums run in double, so a draw can differ from the
-// reference's float sums only when it lands within float rounding of a
-// cumulative boundary.
+// (descending value, ascending index on ties; std::sort leaves the order of
+// exactly equal logits unspecified) with a bitonic sort in shared memory.
+// The exponentials are computed in parallel (double exp rounded to float:
+// the correctly rounded value the reference's std::exp returns in all but
+// rare halfway cases); the normalising sum and the cumulative scans are
+// sequential float additions in the reference's order, so the draw is the
+// reference's.  Sorted-descending scans stop at the first zero term (adding
+// +0 changes nothing).
 // ---------------------------------------------------------------------------
 namespace {
 constexpr int SORT_THREADS = 1024;
@@ -127,29 +131,7 @@ constexpr int SORT_THREADS = 1024;
 __device__ __forceinline__ bool before(float va, int ia, float vb, int ib) {
     return va > vb || (va == vb && ia < ib);
 }
-
-// Inclusive block scan of one double per thread.
-__device__ double block_scan(double v, double* sh) {
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    for (int o = 1; o < 32; o <<= 1) {
-        const double t = __shfl_up_sync(0xffffffffu, v, o);
-        if (lane >= o) v += t;
-    }
-    if (lane == 31) sh[w] = v;
-    __syncthreads();
-    if (w == 0) {
-        double t = (lane < (blockDim.x >> 5)) ? sh[lane] : 0.0;
-        for (int o = 1; o < 32; o <<= 1) {
-            const double u = __shfl_up_sync(0xffffffffu, t, o);
-            if (lane >= o) t += u;
-        }
-        sh[lane] = t;
-    }
-    __syncthreads();
-    const double base = (w > 0) ? sh[w - 1] : 0.0;
-    __syncthreads();
-    return v + base;
-}
+__device__ __forceinline__ float exp_ref(float x) { return (float)exp((double)x); }
 }  // namespace
 
 __global__ void __launch_bounds__(SORT_THREADS) sample_kernel(const float* __restrict__ logits, int ld, int V, int P2,
@@ -159,7 +141,7 @@ __global__ void __launch_bounds__(SORT_THREADS) sample_kernel(const float* __res
     extern __shared__ __align__(16) uint8_t sm[];
     float* key = reinterpret_cast<float*>(sm);
     int* idx = reinterpret_cast<int*>(sm + (size_t)P2 * sizeof(float));
-    __shared__ double sh[32];
+    __shared__ float red[32];
     const int b = blockIdx.x;
     if (b >= n) return;
     const float* lg = logits + (size_t)rows[b] * ld;
@@ -168,41 +150,35 @@ __global__ void __launch_bounds__(SORT_THREADS) sample_kernel(const float* __res
     const bool top_p = cfg.top_p < 1.0f && cfg.top_p > 0.0f;
     const bool top_k = !top_p && cfg.top_k > 0 && (int)cfg.top_k < V;
     const int tid = threadIdx.x;
-    if (!top_p && !top_k) {
-        // temperature sampling over index order
+    if (!top_p && !top_k) {  // temperature sampling in index order (src/engine.cpp:895-915)
         float mx = -INFINITY;
         for (int i = tid; i < V; i += blockDim.x) mx = fmaxf(mx, lg[i]);
         for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if ((tid & 31) == 0) sh[tid >> 5] = mx;
+        if ((tid & 31) == 0) red[tid >> 5] = mx;
         __syncthreads();
-        mx = -INFINITY;
-        for (int w = 0; w < (int)(blockDim.x >> 5); w++) mx = fmaxf(mx, (float)sh[w]);
-        __syncthreads();
-        const int per = ceil_div(V, blockDim.x);
-        double loc = 0.0;
-        for (int j = 0; j < per; j++) {
-            const int i = tid * per + j;
-            if (i < V) loc += (double)expf((lg[i] - mx) / t);
+        if (tid == 0) {
+            float m = red[0];
+            for (int w = 1; w < (int)(blockDim.x >> 5); w++) m = fmaxf(m, red[w]);
+            red[0] = m;
         }
-        const double incl = block_scan(loc, sh);
-        const double total = sh[(blockDim.x >> 5) - 1];
-        double c;
-        // first thread-local hit in index order
-        __shared__ int s_first;
-        if (tid == 0) s_first = 0x7fffffff;
         __syncthreads();
-        c = incl - loc;
-        for (int j = 0; j < per; j++) {
-            const int i = tid * per + j;
-            if (i >= V) break;
-            c += (double)expf((lg[i] - mx) / t);
-            if ((double)u <= c / total) {
-                atomicMin(&s_first, i);
-                break;
+        mx = red[0];
+        for (int i = tid; i < V; i += blockDim.x) key[i] = exp_ref(__fdiv_rn(__fsub_rn(lg[i], mx), t));
+        __syncthreads();
+        if (tid == 0) {
+            float sum = 0.0f;
+            for (int i = 0; i < V; i++) sum = __fadd_rn(sum, key[i]);
+            float cum = 0.0f;
+            int pick = V - 1;
+            for (int i = 0; i < V; i++) {
+                cum = __fadd_rn(cum, __fdiv_rn(key[i], sum));
+                if (u <= cum) {
+                    pick = i;
+                    break;
+                }
             }
+            out[b] = pick;
         }
-        __syncthreads();
-        if (tid == 0) out[b] = (s_first == 0x7fffffff) ? V - 1 : s_first;
         return;
     }
     for (int i = tid; i < P2; i += blockDim.x) {
@@ -215,8 +191,8 @@ __global__ void __launch_bounds__(SORT_THREADS) sample_kernel(const float* __res
             for (int i = tid; i < P2; i += blockDim.x) {
                 const int p = i ^ j;
                 if (p > i) {
-                    const bool up = (i & k) == 0;  // "up" segments sort descending
-                    const bool swap = up ? before(key[p], idx[p], key[i], idx[i]) : before(key[i], idx[i], key[p], idx[p]);
+                    const bool desc = (i & k) == 0;
+                    const bool swap = desc ? before(key[p], idx[p], key[i], idx[i]) : before(key[i], idx[i], key[p], idx[p]);
                     if (swap) {
                         const float tk = key[i];
                         key[i] = key[p];
@@ -231,48 +207,52 @@ __global__ void __launch_bounds__(SORT_THREADS) sample_kernel(const float* __res
         }
     const float mx = key[0];
     const int nn = top_p ? V : (int)cfg.top_k;
-    const int per = ceil_div(nn, blockDim.x);
-    double loc = 0.0;
-    for (int j = 0; j < per; j++) {
-        const int i = tid * per + j;
-        if (i < nn) loc += (double)expf((key[i] - mx) / t);
-    }
-    const double incl = block_scan(loc, sh);
-    const double total = sh[(blockDim.x >> 5) - 1];
-    __shared__ int s_cut, s_pick;
-    if (tid == 0) {
-        s_cut = nn;
-        s_pick = 0x7fffffff;
-    }
     __syncthreads();
-    if (top_p) {
-        double c = incl - loc;
-        for (int j = 0; j < per; j++) {
-            const int i = tid * per + j;
-            if (i >= nn) break;
-            c += (double)expf((key[i] - mx) / t);
-            if (c / total >= (double)cfg.top_p) {
-                atomicMin(&s_cut, i + 1);
+    // exponentials in sorted order, in place (key[i] is no longer needed after this)
+    for (int i = tid; i < nn; i += blockDim.x) key[i] = exp_ref(__fdiv_rn(__fsub_rn(key[i], mx), t));
+    __syncthreads();
+    if (tid != 0) return;
+    float total = 0.0f;
+    int nz = nn;  // terms after the first zero are zero too (sorted descending)
+    for (int i = 0; i < nn; i++) {
+        if (key[i] == 0.0f) {
+            nz = i;
+            break;
+        }
+        total = __fadd_rn(total, key[i]);
+    }
+    if (top_p) {  // src/engine.cpp:972-1002: normalise, cut at cumulative >= p, draw without renormalising
+        int cut = nn;
+        float cum = 0.0f;
+        for (int i = 0; i < nz; i++) {
+            cum = __fadd_rn(cum, __fdiv_rn(key[i], total));
+            if (cum >= cfg.top_p) {
+                cut = i + 1;
                 break;
             }
         }
-        __syncthreads();
-    }
-    const int cut = s_cut;
-    {
-        double c = incl - loc;
-        for (int j = 0; j < per; j++) {
-            const int i = tid * per + j;
-            if (i >= cut) break;
-            c += (double)expf((key[i] - mx) / t);
-            if ((double)u <= c / total) {
-                atomicMin(&s_pick, i);
+        cum = 0.0f;
+        int pick = -1;
+        for (int i = 0; i < min(cut, nz); i++) {
+            cum = __fadd_rn(cum, __fdiv_rn(key[i], total));
+            if (u <= cum) {
+                pick = i;
                 break;
             }
         }
+        out[b] = idx[pick >= 0 ? pick : cut - 1];
+    } else {  // top-k (src/engine.cpp:930-959)
+        float cum = 0.0f;
+        int pick = -1;
+        for (int i = 0; i < nz; i++) {
+            cum = __fadd_rn(cum, __fdiv_rn(key[i], total));
+            if (u <= cum) {
+                pick = i;
+                break;
+            }
+        }
+        out[b] = idx[pick >= 0 ? pick : nn - 1];
     }
-    __syncthreads();
-    if (tid == 0) out[b] = idx[(s_pick == 0x7fffffff) ? cut - 1 : s_pick];
 }
 
 pf_status sample_rows(const float* logits, int ld, int V, const int* rows, int n, const pf_sampling_config& cfg,

@@ -96,9 +96,9 @@ __global__ void kv_pool_spec_kernel(KvCache kv, int layer, RowBatch rb, SpecPool
         const int q0 = kv.S + max(j * kv.pb, E0), q1 = kv.S + (j + 1) * kv.pb;
         for (int q = q0; q < q1; q++) {
             const int slot = (q - kv.S) % kv.Wr;
-            const size_t e = u * kv.W_alloc + slot;
+            const size_t e = u * kv.W_pad + slot;
             sk += (double)kv.ring_k[e * 64 + d] * (double)kv.ring_ks[e];
-            sv += (double)kv.ring_v[e * 64 + d] * (double)kv.ring_vs[e];
+            sv += (double)kv.ring_v[u * kv.W_pad * 64 + kv_voff(slot, d)] * (double)kv.ring_vs[e];
         }
         const float inv = 1.0f / (float)kv.pb;
         const float mk = (float)(sk * (double)inv), mv = (float)(sv * (double)inv);
@@ -146,7 +146,8 @@ constexpr int KROW = 80;     // smem bytes per K row (conflict-free 16 B reads)
 
 struct EntryDesc {
     const int8_t* k;
-    const int8_t* v;
+    const int8_t* v;       // entry-major row, or the unit's blocked V array
+    int vblock;            // >= 0: entry index inside the blocked V array
     float ks, vs;
     int rlo, rhi;  // visible to rows rlo..rhi
 };
@@ -154,6 +155,7 @@ struct EntryDesc {
 __device__ EntryDesc entry_at(const KvCache& kv, int layer, int b, int g, int L0, int n, int row0, int e,
                               int cs, int npool, int nb0, int qlo, int nwin, const Staged& st, const SpecPool& sp) {
     EntryDesc d;
+    d.vblock = -1;
     const size_t u = kv.unit(b, layer, g);
     if (e < cs) {  // committed sink position e
         d.k = kv.sink_k + (u * kv.S + e) * 64;
@@ -167,10 +169,11 @@ __device__ EntryDesc entry_at(const KvCache& kv, int layer, int b, int g, int L0
     e -= cs;
     if (e < npool) {  // pool entry e
         if (e < nb0) {
-            d.k = kv.pool_k + (u * kv.P_max + e) * 64;
-            d.v = kv.pool_v + (u * kv.P_max + e) * 64;
-            d.ks = kv.pool_ks[u * kv.P_max + e];
-            d.vs = kv.pool_vs[u * kv.P_max + e];
+            d.k = kv.pool_k + (u * kv.P_pad + e) * 64;
+            d.v = kv.pool_v + u * kv.P_pad * 64;
+            d.vblock = e;
+            d.ks = kv.pool_ks[u * kv.P_pad + e];
+            d.vs = kv.pool_vs[u * kv.P_pad + e];
         } else {
             const size_t o = ((size_t)b * kv.G + g) * sp.per + (e - nb0);
             d.k = sp.k + o * 64;
@@ -186,9 +189,10 @@ __device__ EntryDesc entry_at(const KvCache& kv, int layer, int b, int g, int L0
     if (e < nwin) {  // committed window position q
         const int q = qlo + e;
         const int slot = (q - kv.S) % kv.Wr;
-        const size_t o = u * kv.W_alloc + slot;
+        const size_t o = u * kv.W_pad + slot;
         d.k = kv.ring_k + o * 64;
-        d.v = kv.ring_v + o * 64;
+        d.v = kv.ring_v + u * kv.W_pad * 64;
+        d.vblock = slot;
         d.ks = kv.ring_ks[o];
         d.vs = kv.ring_vs[o];
         d.rlo = 0;
@@ -257,7 +261,11 @@ __global__ void __launch_bounds__(256) attention_kernel(KvCache kv, int layer, R
                 if (e < T) {
                     const EntryDesc d = entry_at(kv, layer, b, g, L0, n, row0, e, cs, npool, nb0, qlo, nwin, st, sp);
                     *reinterpret_cast<uint4*>(Kt + i * KROW + c * 16) = *reinterpret_cast<const uint4*>(d.k + c * 16);
-                    *reinterpret_cast<uint4*>(Vt + i * 64 + c * 16) = *reinterpret_cast<const uint4*>(d.v + c * 16);
+                    if (d.vblock < 0) {
+                        *reinterpret_cast<uint4*>(Vt + i * 64 + c * 16) = *reinterpret_cast<const uint4*>(d.v + c * 16);
+                    } else {
+                        for (int dd = c * 16; dd < c * 16 + 16; dd++) Vt[i * 64 + dd] = d.v[kv_voff(d.vblock, dd)];
+                    }
                     if (c == 0) {
                         kst[i] = d.ks;
                         vst[i] = d.vs;
@@ -386,10 +394,11 @@ __global__ void kv_commit_kernel(KvCache kv, RowBatch rb, const int* __restrict_
             continue;
         }
         const int slot = (p - kv.S) % kv.Wr;
-        const size_t e = u * kv.W_alloc + slot;
+        const size_t e = u * kv.W_pad + slot;
+        const size_t ve = u * kv.W_pad * 64 + kv_voff(slot, d);
         if (p - kv.S >= kv.Wr) {  // window full: evict position p - Wr from this slot
             ak += (double)kv.ring_k[e * 64 + d] * (double)kv.ring_ks[e];
-            av += (double)kv.ring_v[e * 64 + d] * (double)kv.ring_vs[e];
+            av += (double)kv.ring_v[ve] * (double)kv.ring_vs[e];
             const int E = p - kv.S - kv.Wr + 1;  // evictions so far
             if (E % kv.pb == 0) {
                 const int blk = E / kv.pb - 1;
@@ -409,9 +418,9 @@ __global__ void kv_commit_kernel(KvCache kv, RowBatch rb, const int* __restrict_
                 const float mulk = amk == 0.0f ? 1.0f : __fdiv_rn(127.0f, amk);
                 const float mulv = amv == 0.0f ? 1.0f : __fdiv_rn(127.0f, amv);
                 if (blk < kv.P_max) {
-                    const size_t po = u * kv.P_max + blk;
+                    const size_t po = u * kv.P_pad + blk;
                     kv.pool_k[po * 64 + d] = (int8_t)(int)roundf(__fmul_rn(mk, mulk));
-                    kv.pool_v[po * 64 + d] = (int8_t)(int)roundf(__fmul_rn(mv, mulv));
+                    kv.pool_v[u * kv.P_pad * 64 + kv_voff(blk, d)] = (int8_t)(int)roundf(__fmul_rn(mv, mulv));
                     if (d == 0) {
                         kv.pool_ks[po] = amk == 0.0f ? 1.0f : __fdiv_rn(amk, 127.0f);
                         kv.pool_vs[po] = amv == 0.0f ? 1.0f : __fdiv_rn(amv, 127.0f);
@@ -423,7 +432,7 @@ __global__ void kv_commit_kernel(KvCache kv, RowBatch rb, const int* __restrict_
         }
         __syncthreads();  // every lane has read the old slot
         kv.ring_k[e * 64 + d] = nk;
-        kv.ring_v[e * 64 + d] = nv;
+        kv.ring_v[ve] = nv;
         if (d == 0) {
             kv.ring_ks[e] = nks;
             kv.ring_vs[e] = nvs;

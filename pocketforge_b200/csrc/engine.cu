@@ -169,7 +169,10 @@ struct pf_engine {
             }
             PF_TRY(kv_quant_rows(qkv, NQKV, NQ, NQ + NK, M, nullptr, G, hd, sl, st));
             if (evicting) PF_TRY(kv_pool_spec(kv, l, rb, sp, st));
-            PF_TRY(attention(kv, l, rb, qkv, NQKV, NQ, NQ + NK, H, sl, sp, att, NQ, st));
+            if (attention_decode_supported(H, G, rb.max_rows))
+                PF_TRY(attention_decode(kv, l, rb, qkv, NQKV, NQ, NQ + NK, H, sl, sp, att, NQ, st));
+            else
+                PF_TRY(attention(kv, l, rb, qkv, NQKV, NQ, NQ + NK, H, sl, sp, att, NQ, st));
             PF_TRY(quant_rows(att, NQ, NQ, M, nullptr, xq, xs, NQ, st));
             {
                 GemmParams p;
@@ -440,22 +443,33 @@ pf_status pf_engine_create(const pf_model_config* c, int32_t max_seqs, int32_t m
     kv.Wr = std::min(c->window_size, c->max_context);
     kv.W_alloc = std::max(1, std::min(kv.Wr, max_positions - kv.S));
     kv.P_max = (max_positions - kv.S - kv.Wr > 0) ? (max_positions - kv.S - kv.Wr) / kv.pb + 1 : 1;
+    kv.W_pad = ceil_div(kv.W_alloc, 32) * 32;
+    kv.P_pad = ceil_div(kv.P_max, 32) * 32;
     e->evicting = max_positions - kv.S > kv.Wr;
     const size_t units = (size_t)max_seqs * L * G;
-    E_TRY(dalloc(&kv.ring_k, units * kv.W_alloc * 64, o));
-    E_TRY(dalloc(&kv.ring_v, units * kv.W_alloc * 64, o));
-    E_TRY(dalloc(&kv.ring_ks, units * kv.W_alloc, o));
-    E_TRY(dalloc(&kv.ring_vs, units * kv.W_alloc, o));
+    E_TRY(dalloc(&kv.ring_k, units * kv.W_pad * 64, o));
+    E_TRY(dalloc(&kv.ring_v, units * kv.W_pad * 64, o));
+    E_TRY(dalloc(&kv.ring_ks, units * kv.W_pad, o));
+    E_TRY(dalloc(&kv.ring_vs, units * kv.W_pad, o));
     E_TRY(dalloc(&kv.sink_k, units * std::max(1, kv.S) * 64, o));
     E_TRY(dalloc(&kv.sink_v, units * std::max(1, kv.S) * 64, o));
     E_TRY(dalloc(&kv.sink_ks, units * std::max(1, kv.S), o));
     E_TRY(dalloc(&kv.sink_vs, units * std::max(1, kv.S), o));
-    E_TRY(dalloc(&kv.pool_k, units * kv.P_max * 64, o));
-    E_TRY(dalloc(&kv.pool_v, units * kv.P_max * 64, o));
-    E_TRY(dalloc(&kv.pool_ks, units * kv.P_max, o));
-    E_TRY(dalloc(&kv.pool_vs, units * kv.P_max, o));
+    E_TRY(dalloc(&kv.pool_k, units * kv.P_pad * 64, o));
+    E_TRY(dalloc(&kv.pool_v, units * kv.P_pad * 64, o));
+    E_TRY(dalloc(&kv.pool_ks, units * kv.P_pad, o));
+    E_TRY(dalloc(&kv.pool_vs, units * kv.P_pad, o));
     E_TRY(dalloc(&kv.acc_k, units * 64, o));
     E_TRY(dalloc(&kv.acc_v, units * 64, o));
+    // zero-filled so that padding slots read by whole-block loads hold finite values
+    PF_CUDA(cudaMemset(kv.ring_k, 0, units * kv.W_pad * 64));
+    PF_CUDA(cudaMemset(kv.ring_v, 0, units * kv.W_pad * 64));
+    PF_CUDA(cudaMemset(kv.ring_ks, 0, units * kv.W_pad * 4));
+    PF_CUDA(cudaMemset(kv.ring_vs, 0, units * kv.W_pad * 4));
+    PF_CUDA(cudaMemset(kv.pool_k, 0, units * kv.P_pad * 64));
+    PF_CUDA(cudaMemset(kv.pool_v, 0, units * kv.P_pad * 64));
+    PF_CUDA(cudaMemset(kv.pool_ks, 0, units * kv.P_pad * 4));
+    PF_CUDA(cudaMemset(kv.pool_vs, 0, units * kv.P_pad * 4));
 
     // activations
     const size_t Mc = e->Mcap;
@@ -989,13 +1003,26 @@ pf_status pf_engine_read_kv(pf_engine* e, int32_t b, int32_t l, int32_t g, int8_
     for (int p = 0; p < cs; p++)
         PF_TRY(put(kv.sink_k + (u * kv.S + p) * 64, kv.sink_ks + u * kv.S + p, kv.sink_v + (u * kv.S + p) * 64,
                    kv.sink_vs + u * kv.S + p));
+    std::vector<int8_t> vblk(64 * 32);
+    auto put_blocked = [&](const int8_t* kp, const float* ksp, const int8_t* vbase, size_t e, const float* vsp)
+        -> pf_status {
+        if (n >= max_entries) return PF_OK;
+        PF_CUDA(cudaMemcpy(k + (size_t)n * 64, kp, 64, cudaMemcpyDeviceToHost));
+        PF_CUDA(cudaMemcpy(vblk.data(), vbase + (e >> 5) * 2048, 2048, cudaMemcpyDeviceToHost));
+        for (int d = 0; d < 64; d++) v[(size_t)n * 64 + d] = vblk[(size_t)d * 32 + kv_vpos((int)(e & 31))];
+        PF_CUDA(cudaMemcpy(ks + n, ksp, 4, cudaMemcpyDeviceToHost));
+        PF_CUDA(cudaMemcpy(vs + n, vsp, 4, cudaMemcpyDeviceToHost));
+        n++;
+        return PF_OK;
+    };
     for (int j = 0; j < np; j++)
-        PF_TRY(put(kv.pool_k + (u * kv.P_max + j) * 64, kv.pool_ks + u * kv.P_max + j,
-                   kv.pool_v + (u * kv.P_max + j) * 64, kv.pool_vs + u * kv.P_max + j));
+        PF_TRY(put_blocked(kv.pool_k + (u * kv.P_pad + j) * 64, kv.pool_ks + u * kv.P_pad + j,
+                           kv.pool_v + u * kv.P_pad * 64, (size_t)j, kv.pool_vs + u * kv.P_pad + j));
     for (int i = 0; i < nw; i++) {
         const int slot = (qlo + i - kv.S) % kv.Wr;
-        const size_t o = u * kv.W_alloc + slot;
-        PF_TRY(put(kv.ring_k + o * 64, kv.ring_ks + o, kv.ring_v + o * 64, kv.ring_vs + o));
+        const size_t o = u * kv.W_pad + slot;
+        PF_TRY(put_blocked(kv.ring_k + o * 64, kv.ring_ks + o, kv.ring_v + u * kv.W_pad * 64, (size_t)slot,
+                           kv.ring_vs + o));
     }
     *count = n;
     return PF_OK;

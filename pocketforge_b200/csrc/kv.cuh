@@ -16,20 +16,31 @@
 
 namespace pf {
 
+// K rows are stored entry-major ([slot][64]).  V is stored dim-major per block
+// of 32 slots: block b holds [64 dims][32 bytes] and the byte of slot
+// 32b + i sits at position kv_vpos(i) of its dim row — the order in which the
+// tensor-core attention consumes entries (attn_decode.cu).
 struct KvCache {
     int n_seqs = 0, L = 0, G = 0, hd = 64;
     int S = 4, Wr = 0, W_alloc = 0, P_max = 0, pb = 64, max_pos = 0;
-    int8_t *ring_k = nullptr, *ring_v = nullptr;  // [unit][W_alloc][hd]
-    float *ring_ks = nullptr, *ring_vs = nullptr; // [unit][W_alloc]
-    int8_t *sink_k = nullptr, *sink_v = nullptr;  // [unit][S][hd]
+    int W_pad = 0, P_pad = 0;                     // W_alloc, P_max rounded up to 32
+    int8_t *ring_k = nullptr, *ring_v = nullptr;  // [unit][W_pad][hd] (V in blocks, see above)
+    float *ring_ks = nullptr, *ring_vs = nullptr; // [unit][W_pad]
+    int8_t *sink_k = nullptr, *sink_v = nullptr;  // [unit][S][hd] entry-major
     float *sink_ks = nullptr, *sink_vs = nullptr;
-    int8_t *pool_k = nullptr, *pool_v = nullptr;  // [unit][P_max][hd]
+    int8_t *pool_k = nullptr, *pool_v = nullptr;  // [unit][P_pad][hd] (V in blocks)
     float *pool_ks = nullptr, *pool_vs = nullptr;
     double *acc_k = nullptr, *acc_v = nullptr;    // [unit][hd]
     __host__ __device__ size_t unit(int seq, int layer, int g) const {
         return ((size_t)seq * L + layer) * G + g;
     }
 };
+
+__host__ __device__ inline int kv_vpos(int i) { return ((i & 7) >> 1) * 8 + (i >> 3) * 2 + (i & 1); }
+// Byte offset of (entry e, dim d) inside a [n][64] V array stored in blocks.
+__host__ __device__ inline size_t kv_voff(size_t e, int d) {
+    return (e >> 5) * 2048 + (size_t)d * 32 + kv_vpos((int)(e & 31));
+}
 
 __host__ __device__ inline int kv_pool_count(int len, int S, int Wr, int pb) {
     const int e = len - S - Wr;
@@ -66,6 +77,10 @@ pf_status kv_quant_rows(const float* qkv, int ldqkv, int k_col, int v_col, int M
 pf_status kv_pool_spec(const KvCache& kv, int layer, const RowBatch& rb, SpecPool sp, cudaStream_t stream);
 pf_status attention(const KvCache& kv, int layer, const RowBatch& rb, const float* qkv, int ldqkv, int k_col,
                     int v_col, int H, Staged st, SpecPool sp, float* out, int ldo, cudaStream_t stream);
+// Tensor-core variant for batches of at most 32 / (H/G) rows per sequence.
+bool attention_decode_supported(int H, int G, int max_rows);
+pf_status attention_decode(const KvCache& kv, int layer, const RowBatch& rb, const float* qkv, int ldqkv, int k_col,
+                           int v_col, int H, Staged st, SpecPool sp, float* out, int ldo, cudaStream_t stream);
 // Commits rows [0, n_commit[b]) of every sequence into the cache, all layers.
 // `staged` holds layer 0; layer l is at +l*M*G*hd (int8) and +l*M*G (scales).
 pf_status kv_commit(const KvCache& kv, const RowBatch& rb, const int* n_commit, Staged staged, int M_stride,

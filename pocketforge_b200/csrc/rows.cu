@@ -2,15 +2,22 @@
 // activation quantization, the 3-digit split of fp32 rows for the exact-int
 // tensor-core unembed, embedding gather, argmax, softmax.
 //
-// One warp per row.  RMSNorm's sum of squares uses a fixed order ("device
-// order"): lane l sums elements l, l+32, ... sequentially, then an xor
-// butterfly over offsets 16..1; oracle/pf_oracle.cpp restates the same order
-// (order=1) so the GPU result can be checked bit for bit, and the reference's
-// sequential order (order=0) within tolerance.
+// One CTA of 256 threads per row; thread t keeps elements t, t+256, ... in
+// registers, so each row is read from memory once.  RMSNorm's sum of squares
+// uses a fixed order ("device order"): every thread sums its elements in
+// sequence, each warp combines its threads with an xor butterfly over offsets
+// 16..1, and thread 0 adds the 8 warp totals in warp order.
+// oracle/pf_oracle.cpp restates this order (order=1) so the GPU result is
+// checked bit for bit, and the reference's sequential order (order=0) within
+// tolerance.
 #include "common.cuh"
 #include "rows.cuh"
 
 namespace pf {
+
+namespace {
+constexpr int RT = 256;      // threads per row
+constexpr int EPT = 24;      // elements per thread held in registers (n <= 6144)
 
 __device__ __forceinline__ float warp_sum_xor(float v) {
 #pragma unroll
@@ -22,80 +29,136 @@ __device__ __forceinline__ float warp_max(float v) {
     for (int o = 16; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
 }
+// Block sum in the device order; every thread gets the result.
+__device__ __forceinline__ float block_sum(float v, float* sh) {
+    v = warp_sum_xor(v);
+    const int w = threadIdx.x >> 5;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) sh[w] = v;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = sh[0];
+        for (int i = 1; i < (int)(blockDim.x >> 5); i++) t = __fadd_rn(t, sh[i]);
+        sh[32] = t;
+    }
+    __syncthreads();
+    return sh[32];
+}
+__device__ __forceinline__ float block_max(float v, float* sh) {
+    v = warp_max(v);
+    const int w = threadIdx.x >> 5;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) sh[w] = v;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = sh[0];
+        for (int i = 1; i < (int)(blockDim.x >> 5); i++) t = fmaxf(t, sh[i]);
+        sh[32] = t;
+    }
+    __syncthreads();
+    return sh[32];
+}
 
-// quantize_activation_row (src/matmul_neon.cpp:16-29) of a row already in
-// registers / memory: amax, mul = 127/amax, q = round(x*mul), scale = amax/127.
+// quantize_activation_row (src/matmul_neon.cpp:16-29): mul = 127/amax,
+// q = round(x*mul) (half away from zero), scale = amax/127; 1 for zero rows.
 __device__ __forceinline__ void row_quant_params(float amax, float& mul, float& scale) {
     mul = (amax == 0.0f) ? 1.0f : __fdiv_rn(127.0f, amax);
     scale = (amax == 0.0f) ? 1.0f : __fdiv_rn(amax, 127.0f);
 }
 __device__ __forceinline__ int8_t q8(float x, float mul) { return (int8_t)(int)roundf(__fmul_rn(x, mul)); }
 
+__device__ __forceinline__ bool row_active(int row, int M, const int* m_dev) {
+    return row < (m_dev ? min(M, *m_dev) : M);
+}
+}  // namespace
+
 // ---------------------------------------------------------------------------
 // RMSNorm (src/matmul_neon.cpp:231-239) fused with the activation quantizer.
 // normed (optional) receives the fp32 output; q/qs the int8 row and scale.
 // ---------------------------------------------------------------------------
-__global__ void rmsnorm_quant_kernel(const float* __restrict__ x, const float* __restrict__ w, int n,
-                                     float eps, int M, const int* m_dev, float* __restrict__ normed,
-                                     int8_t* __restrict__ q, float* __restrict__ qs, int ldq) {
-    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    const int m_act = m_dev ? min(M, *m_dev) : M;
-    if (row >= m_act) return;
+__global__ void __launch_bounds__(RT) rmsnorm_quant_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                           int n, float eps, int M, const int* m_dev,
+                                                           float* __restrict__ normed, int8_t* __restrict__ q,
+                                                           float* __restrict__ qs, int ldq) {
+    __shared__ float sh[33];
+    const int row = blockIdx.x, t = threadIdx.x;
+    if (!row_active(row, M, m_dev)) return;
     const float* xr = x + (size_t)row * n;
+    float v[EPT];
     float ss = 0.0f;
-    for (int i = lane; i < n; i += 32) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
-    ss = warp_sum_xor(ss);
-    const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps));
-    const float inv = __fdiv_rn(1.0f, rms);
-    float amax = 0.0f;
-    for (int i = lane; i < n; i += 32) {
-        const float v = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
-        if (normed) normed[(size_t)row * n + i] = v;
-        amax = fmaxf(amax, fabsf(v));
+#pragma unroll
+    for (int i = 0; i < EPT; i++) {
+        const int c = t + i * RT;
+        v[i] = c < n ? xr[c] : 0.0f;
+        ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
     }
-    amax = warp_max(amax);
+    ss = block_sum(ss, sh);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < EPT; i++) {
+        const int c = t + i * RT;
+        if (c < n) {
+            v[i] = __fmul_rn(__fmul_rn(v[i], inv), w[c]);
+            if (normed) normed[(size_t)row * n + c] = v[i];
+            amax = fmaxf(amax, fabsf(v[i]));
+        }
+    }
     if (!q) return;
+    amax = block_max(amax, sh);
     float mul, scale;
     row_quant_params(amax, mul, scale);
-    for (int i = lane; i < n; i += 32) {
-        const float v = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
-        q[(size_t)row * ldq + i] = q8(v, mul);
+#pragma unroll
+    for (int i = 0; i < EPT; i++) {
+        const int c = t + i * RT;
+        if (c < n) q[(size_t)row * ldq + c] = q8(v[i], mul);
     }
-    if (lane == 0) qs[row] = scale;
+    if (t == 0) qs[row] = scale;
 }
 
-pf_status rmsnorm_quant(const float* x, const float* w, int n, float eps, int M, const int* m_dev,
-                        float* normed, int8_t* q, float* qs, int ldq, cudaStream_t st) {
-    const int rows_per_block = 4;
-    rmsnorm_quant_kernel<<<ceil_div(M, rows_per_block), 32 * rows_per_block, 0, st>>>(
-        x, w, n, eps, M, m_dev, normed, q, qs, ldq);
+pf_status rmsnorm_quant(const float* x, const float* w, int n, float eps, int M, const int* m_dev, float* normed,
+                        int8_t* q, float* qs, int ldq, cudaStream_t st) {
+    PF_CHECK(n <= RT * EPT, "rmsnorm_quant: row length %d above %d", n, RT * EPT);
+    rmsnorm_quant_kernel<<<M, RT, 0, st>>>(x, w, n, eps, M, m_dev, normed, q, qs, ldq);
     return launch_check("rmsnorm_quant");
 }
 
 // ---------------------------------------------------------------------------
-// quantize_activation_row over M rows.
+// quantize_activation_row over M rows (any length: rows longer than the
+// register cache take a second pass over memory).
 // ---------------------------------------------------------------------------
-__global__ void quant_rows_kernel(const float* __restrict__ x, int n, int ldx, int M, const int* m_dev,
-                                  int8_t* __restrict__ q, float* __restrict__ qs, int ldq) {
-    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    const int m_act = m_dev ? min(M, *m_dev) : M;
-    if (row >= m_act) return;
+__global__ void __launch_bounds__(RT) quant_rows_kernel(const float* __restrict__ x, int n, int ldx, int M,
+                                                        const int* m_dev, int8_t* __restrict__ q, float* __restrict__ qs,
+                                                        int ldq) {
+    __shared__ float sh[33];
+    const int row = blockIdx.x, t = threadIdx.x;
+    if (!row_active(row, M, m_dev)) return;
     const float* xr = x + (size_t)row * ldx;
+    float v[EPT];
     float amax = 0.0f;
-    for (int i = lane; i < n; i += 32) amax = fmaxf(amax, fabsf(xr[i]));
-    amax = warp_max(amax);
+#pragma unroll
+    for (int i = 0; i < EPT; i++) {
+        const int c = t + i * RT;
+        v[i] = c < n ? xr[c] : 0.0f;
+        amax = fmaxf(amax, fabsf(v[i]));
+    }
+    for (int c = t + EPT * RT; c < n; c += RT) amax = fmaxf(amax, fabsf(xr[c]));
+    amax = block_max(amax, sh);
     float mul, scale;
     row_quant_params(amax, mul, scale);
     int8_t* qr = q + (size_t)row * ldq;
-    for (int i = lane; i < n; i += 32) qr[i] = q8(xr[i], mul);
-    if (lane == 0) qs[row] = scale;
+#pragma unroll
+    for (int i = 0; i < EPT; i++) {
+        const int c = t + i * RT;
+        if (c < n) qr[c] = q8(v[i], mul);
+    }
+    for (int c = t + EPT * RT; c < n; c += RT) qr[c] = q8(xr[c], mul);
+    if (t == 0) qs[row] = scale;
 }
 
 pf_status quant_rows(const float* x, int n, int ldx, int M, const int* m_dev, int8_t* q, float* qs, int ldq,
                      cudaStream_t st) {
-    quant_rows_kernel<<<ceil_div(M, 4), 128, 0, st>>>(x, n, ldx, M, m_dev, q, qs, ldq);
+    quant_rows_kernel<<<M, RT, 0, st>>>(x, n, ldx, M, m_dev, q, qs, ldq);
     return launch_check("quant_rows");
 }
 
@@ -123,35 +186,47 @@ pf_status quant_rows_given(const float* x, int n, int M, const float* s, int8_t*
 // x ~= s*(q1 + q2/254 + q3/254^2) to ~2^-23 of amax.  Integer MMAs over the
 // planes then reproduce an fp32 dot product to ~1e-7 relative.
 // ---------------------------------------------------------------------------
-__global__ void split_digits_kernel(const float* __restrict__ x, int n, int ldx, int M, const int* m_dev,
-                                    int8_t* __restrict__ q, int64_t plane, int ldq, float* __restrict__ qs) {
-    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    const int m_act = m_dev ? min(M, *m_dev) : M;
-    if (row >= m_act) return;
+__global__ void __launch_bounds__(RT) split_digits_kernel(const float* __restrict__ x, int n, int ldx, int M,
+                                                          const int* m_dev, int8_t* __restrict__ q, int64_t plane,
+                                                          int ldq, float* __restrict__ qs) {
+    __shared__ float sh[33];
+    const int row = blockIdx.x, t = threadIdx.x;
+    if (!row_active(row, M, m_dev)) return;
     const float* xr = x + (size_t)row * ldx;
+    float v[EPT];
     float amax = 0.0f;
-    for (int i = lane; i < n; i += 32) amax = fmaxf(amax, fabsf(xr[i]));
-    amax = warp_max(amax);
-    const float mul = (amax == 0.0f) ? 0.0f : __fdiv_rn(127.0f, amax);
-    for (int i = lane; i < n; i += 32) {
-        const float r0 = __fmul_rn(xr[i], mul);
+#pragma unroll
+    for (int i = 0; i < EPT; i++) {
+        const int c = t + i * RT;
+        v[i] = c < n ? xr[c] : 0.0f;
+        amax = fmaxf(amax, fabsf(v[i]));
+    }
+    amax = block_max(amax, sh);
+    const float mul = (amax == 0.0f || !isfinite(amax)) ? 0.0f : __fdiv_rn(127.0f, amax);
+#pragma unroll
+    for (int i = 0; i < EPT; i++) {
+        const int c = t + i * RT;
+        if (c >= n) continue;
+        const float r0 = __fmul_rn(v[i], mul);
         const float d1 = rintf(r0);
         const float r1 = __fmul_rn(__fsub_rn(r0, d1), 254.0f);
         const float d2 = rintf(r1);
         const float r2 = __fmul_rn(__fsub_rn(r1, d2), 254.0f);
         const float d3 = fminf(127.0f, fmaxf(-127.0f, rintf(r2)));
-        const size_t o = (size_t)row * ldq + i;
+        const size_t o = (size_t)row * ldq + c;
         q[o] = (int8_t)(int)d1;
         q[o + plane] = (int8_t)(int)d2;
         q[o + 2 * plane] = (int8_t)(int)d3;
     }
-    if (lane == 0) qs[row] = (amax == 0.0f) ? 1.0f : __fdiv_rn(amax, 127.0f);
+    // A row that overflowed float range gives NaN products, as the reference's
+    // fp32 dot products over it do (inf * 0 and inf - inf terms).
+    if (t == 0) qs[row] = !isfinite(amax) ? __int_as_float(0x7fc00000) : (amax == 0.0f) ? 1.0f : __fdiv_rn(amax, 127.0f);
 }
 
 pf_status split_digits(const float* x, int n, int ldx, int M, const int* m_dev, int8_t* q, int64_t plane,
                        int ldq, float* qs, cudaStream_t st) {
-    split_digits_kernel<<<ceil_div(M, 4), 128, 0, st>>>(x, n, ldx, M, m_dev, q, plane, ldq, qs);
+    PF_CHECK(n <= RT * EPT, "split_digits: row length %d above %d", n, RT * EPT);
+    split_digits_kernel<<<M, RT, 0, st>>>(x, n, ldx, M, m_dev, q, plane, ldq, qs);
     return launch_check("split_digits");
 }
 
@@ -235,21 +310,22 @@ pf_status argmax_rows(const float* v, int n, int ld, int M, const int* m_dev, in
 // ---------------------------------------------------------------------------
 // Reference-interface helpers (kernel-level C ABI only).
 // ---------------------------------------------------------------------------
-__global__ void rmsnorm_rows_kernel(float* __restrict__ out, const float* __restrict__ x, const float* __restrict__ w,
-                                    int M, int n) {
-    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
+// forge::rmsnorm over rows of any length, in the device order of rmsnorm_quant.
+__global__ void __launch_bounds__(RT) rmsnorm_rows_kernel(float* __restrict__ out, const float* __restrict__ x,
+                                                          const float* __restrict__ w, int M, int n) {
+    __shared__ float sh[33];
+    const int row = blockIdx.x, t = threadIdx.x;
     if (row >= M) return;
     const float* xr = x + (size_t)row * n;
     float ss = 0.0f;
-    for (int i = lane; i < n; i += 32) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
-    ss = warp_sum_xor(ss);
+    for (int c = t; c < n; c += RT) ss = __fadd_rn(ss, __fmul_rn(xr[c], xr[c]));
+    ss = block_sum(ss, sh);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), 1e-6f)));
-    for (int i = lane; i < n; i += 32) out[(size_t)row * n + i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+    for (int c = t; c < n; c += RT) out[(size_t)row * n + c] = __fmul_rn(__fmul_rn(xr[c], inv), w[c]);
 }
 
 pf_status rmsnorm_rows(float* out, const float* x, const float* w, int M, int n, cudaStream_t st) {
-    rmsnorm_rows_kernel<<<ceil_div(M, 4), 128, 0, st>>>(out, x, w, M, n);
+    rmsnorm_rows_kernel<<<M, RT, 0, st>>>(out, x, w, M, n);
     return launch_check("rmsnorm_rows");
 }
 

