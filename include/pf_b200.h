@@ -162,6 +162,20 @@ PF_API pf_status pf_gemm_packed(const int8_t* Aq, const float* a_scale,
                          const void* packed_w, const float* w_scale, int32_t qtype,
                          float* C, int32_t M, int32_t N, int32_t K, void* stream);
 
+/* pf_gemm_packed without any allocation: the same projection, computed with a
+ * split-K reduction whose int32 partial sums live in a fixed array inside the
+ * library (no counterpart in the reference, which has no device memory).
+ * For callers that cannot call cudaMalloc — a runtime whose own pool owns all
+ * device memory, or a path that must not risk the device synchronisation an
+ * allocation can cause.  Limits: M*N <= 1,048,576 and ceil(M/64)*(N/64) <=
+ * 4096 (else PF_ERR_INVALID).  Every GPU that loads the library holds the
+ * 4 MiB array until exit; calls share it, so calls that overlap on the GPU
+ * race.  The first call on a device sets the array up synchronously: make it
+ * before any stream capture. */
+PF_API pf_status pf_gemm_packed_static(const int8_t* Aq, const float* a_scale, const void* packed_w,
+                                       const float* w_scale, int32_t qtype, float* C, int32_t M, int32_t N,
+                                       int32_t K, void* stream);
+
 /* ------------------------------------------------------------------ */
 /* Engine: batched MTP speculative decoding                             */
 /* (Engine::generate / forward_with_hidden / MTPHeads::forward,         */

@@ -1,0 +1,96 @@
+// static_ws.cu — pf_gemm_packed_static: the packed-weight projection kernel
+// with its split-K scratch inside the library image instead of in memory the
+// library or the caller allocates.
+//
+// Who needs it: a host runtime that owns every byte of device memory through
+// its own pool (and forbids other allocators), or a latency-critical path
+// that must not allocate because cudaMalloc can synchronise the device.  Such
+// callers still pass their own input and output buffers; the only extra
+// memory the kernel needs — int32 partial sums and per-tile counters of the
+// split-K reduction — is the file-scope array below.
+//
+// The array is a fixed part of the module: every GPU that loads the library
+// holds it (kStaticWsElems * 4 + kStaticCounters * 4 bytes) until the process
+// exits.  All calls on a device share it and it keeps the last call's
+// contents, so each call clears the part it uses on the caller's stream
+// before launching; two calls whose work overlaps on the GPU (different
+// streams, no ordering between them) race on it and must not be issued.
+// The first call on a device looks up the array's device address
+// (cudaGetSymbolAddress) and clears it synchronously; make that first call
+// before any stream capture.
+#include <mutex>
+
+#include "gemm.cuh"
+
+namespace pf {
+namespace {
+
+constexpr size_t kStaticWsElems = (size_t)1 << 20;  // int32 partial sums: M*N <= 1,048,576
+constexpr int kStaticCounters = 4096;                // split-K tiles: ceil(M/64)*(N/64) <= 4096
+
+static __device__ __align__(256) int32_t g_split_ws[kStaticWsElems];
+static __device__ __align__(256) int g_split_cnt[kStaticCounters];
+
+struct StaticAddr {
+    int32_t* ws = nullptr;
+    int* cnt = nullptr;
+};
+
+pf_status static_addr(StaticAddr* out) {
+    static std::mutex mu;
+    static StaticAddr addr[64];
+    int dev = 0;
+    PF_CUDA(cudaGetDevice(&dev));
+    PF_CHECK(dev >= 0 && dev < 64, "device index %d out of range", dev);
+    std::lock_guard<std::mutex> lk(mu);
+    if (!addr[dev].ws) {
+        // In host code g_split_ws names a host-side shadow, not device memory:
+        // the kernel gets the address the device sees.
+        void* ws = nullptr;
+        void* cnt = nullptr;
+        PF_CUDA(cudaGetSymbolAddress(&ws, g_split_ws));
+        PF_CUDA(cudaGetSymbolAddress(&cnt, g_split_cnt));
+        PF_CUDA(cudaMemset(ws, 0, kStaticWsElems * sizeof(int32_t)));
+        PF_CUDA(cudaMemset(cnt, 0, kStaticCounters * sizeof(int)));
+        PF_CUDA(cudaDeviceSynchronize());
+        addr[dev].ws = static_cast<int32_t*>(ws);
+        addr[dev].cnt = static_cast<int*>(cnt);
+    }
+    *out = addr[dev];
+    return PF_OK;
+}
+
+}  // namespace
+}  // namespace pf
+
+using namespace pf;
+
+extern "C" pf_status pf_gemm_packed_static(const int8_t* Aq, const float* a_scale, const void* packed_w,
+                                           const float* w_scale, int32_t qtype, float* C, int32_t M, int32_t N,
+                                           int32_t K, void* stream) {
+    PF_TRY(require_device());
+    PF_CHECK(Aq && a_scale && packed_w && C, "pf_gemm_packed_static: null argument");
+    PF_CHECK(M > 0 && N > 0 && K > 0, "pf_gemm_packed_static: empty shape");
+    PF_CHECK((size_t)M * (size_t)N <= kStaticWsElems,
+             "pf_gemm_packed_static: M*N = %lld exceeds the static workspace of %zu partial sums",
+             (long long)M * N, kStaticWsElems);
+    PF_CHECK(gemm_counter_count(M, N) <= (size_t)kStaticCounters,
+             "pf_gemm_packed_static: %zu output tiles exceed the %d static tile counters", gemm_counter_count(M, N),
+             kStaticCounters);
+    StaticAddr a;
+    PF_TRY(static_addr(&a));
+    cudaStream_t st = as_stream(stream);
+    GemmParams p;
+    p.A = Aq; p.lda = K; p.a_scale = a_scale; p.M = M; p.N = N; p.K = K;
+    p.W = packed_w; p.wf = wfmt_of_qtype(qtype); p.w_scale = w_scale;
+    p.epi = EPI_F32; p.out = C; p.ldo = N;
+    p.splits = std::max(2, gemm_pick_splits(M, N, K, true));
+    if (K / 128 < 2) p.splits = 1;
+    p.ws = a.ws;
+    p.counters = a.cnt;
+    // The kernel leaves the workspace zeroed, but an earlier call that did not
+    // complete may not have: clear what this call reads before its first use.
+    PF_CUDA(cudaMemsetAsync(a.ws, 0, (size_t)M * N * sizeof(int32_t), st));
+    PF_CUDA(cudaMemsetAsync(a.cnt, 0, gemm_counter_count(M, N) * sizeof(int), st));
+    return gemm_launch(p, 1, st);
+}
