@@ -10,6 +10,7 @@
 
 #include "common.cuh"
 #include "gemm.cuh"
+#include "gemm_tc.cuh"
 #include "rows.cuh"
 #include "step.cuh"
 
@@ -72,7 +73,7 @@ pf_status pf_dequant_ternary_to_int8(const uint8_t* src, int8_t* dst, int64_t n,
 pf_status pf_pack_weights(const int8_t* w, int32_t rows, int32_t cols, int32_t qtype, void* packed, void* stream) {
     PF_TRY(require_device());
     PF_CHECK(qtype >= 0 && qtype <= 3, "pf_pack_weights: bad qtype %d", qtype);
-    return pack_weights(w, rows, cols, wfmt_of_qtype(qtype), packed, as_stream(stream));
+    return pack_weights_tc(w, rows, cols, wfmt_of_qtype(qtype), packed, as_stream(stream));
 }
 
 pf_status pf_gemm_packed(const int8_t* Aq, const float* a_scale, const void* packed_w, const float* w_scale,
@@ -83,7 +84,7 @@ pf_status pf_gemm_packed(const int8_t* Aq, const float* a_scale, const void* pac
     p.A = Aq; p.lda = K; p.a_scale = a_scale; p.M = M; p.N = N; p.K = K;
     p.W = packed_w; p.wf = wfmt_of_qtype(qtype); p.w_scale = w_scale;
     p.epi = EPI_F32; p.out = C; p.ldo = N;
-    return gemm_launch(p, 1, as_stream(stream));
+    return gemm_tc_launch(p, 1, M, as_stream(stream));
 }
 
 pf_status pf_matmul_int8(const int8_t* A, const int8_t* B, int32_t* C, int32_t M, int32_t N, int32_t K,

@@ -3,6 +3,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "gemm_tc.cuh"
 
 namespace pf {
 
@@ -77,5 +78,5 @@ extern "C" int32_t pf_device_count(void) {
 
 extern "C" size_t pf_packed_weight_bytes(int32_t rows, int32_t cols, int32_t qtype) {
     if (rows <= 0 || cols <= 0) return 0;
-    return pf::packed_bytes(rows, cols, pf::wfmt_of_qtype(qtype));
+    return pf::packed_bytes_tc(rows, cols, pf::wfmt_of_qtype(qtype));
 }

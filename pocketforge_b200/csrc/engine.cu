@@ -20,6 +20,7 @@
 
 #include "common.cuh"
 #include "gemm.cuh"
+#include "gemm_tc.cuh"
 #include "kv.cuh"
 #include "rows.cuh"
 #include "step.cuh"
@@ -140,12 +141,15 @@ struct pf_engine {
         return t;
     }
 
+    // Projections run on the tcgen05 kernel (gemm_tc.cu); digit-plane
+    // activations are laid out [3][Mcap][lda].
     pf_status gemm(GemmParams p, int planes) {
-        p.splits = gemm_pick_splits(p.M, p.N, p.K, true);
-        if ((size_t)planes * p.M * p.N > gws_elems || gemm_counter_count(p.M, p.N) > gcnt_elems) p.splits = 1;
+        p.splits = 0;
         p.ws = gws;
         p.counters = gcnt;
-        return gemm_launch(p, planes, st);
+        p.ws_elems = gws_elems;
+        p.cnt_elems = gcnt_elems;
+        return gemm_tc_launch(p, planes, Mcap, st);
     }
 
     // ---- one pass of all layers over a row batch ---------------------------------
@@ -386,10 +390,10 @@ pf_status pf_engine_create(const pf_model_config* c, int32_t max_seqs, int32_t m
     e->loaded.assign(L, 0);
     for (int l = 0; l < L; l++) {
         uint8_t* p;
-        E_TRY(dalloc(&p, packed_bytes(e->NQKV, d, e->fmt_qkv), o)); e->w_qkv[l] = p;
-        E_TRY(dalloc(&p, packed_bytes(d, e->NQ, e->fmt_o), o)); e->w_o[l] = p;
-        E_TRY(dalloc(&p, packed_bytes(2 * F, d, e->fmt_gu), o)); e->w_gu[l] = p;
-        E_TRY(dalloc(&p, packed_bytes(d, F, e->fmt_down), o)); e->w_down[l] = p;
+        E_TRY(dalloc(&p, packed_bytes_tc(e->NQKV, d, e->fmt_qkv), o)); e->w_qkv[l] = p;
+        E_TRY(dalloc(&p, packed_bytes_tc(d, e->NQ, e->fmt_o), o)); e->w_o[l] = p;
+        E_TRY(dalloc(&p, packed_bytes_tc(2 * F, d, e->fmt_gu), o)); e->w_gu[l] = p;
+        E_TRY(dalloc(&p, packed_bytes_tc(d, F, e->fmt_down), o)); e->w_down[l] = p;
         E_TRY(dalloc(&e->s_qkv[l], e->NQKV, o));
         E_TRY(dalloc(&e->s_o[l], d, o));
         E_TRY(dalloc(&e->s_gu[l], 2 * F, o));
@@ -398,7 +402,7 @@ pf_status pf_engine_create(const pf_model_config* c, int32_t max_seqs, int32_t m
     E_TRY(dalloc(&e->emb_i8, (size_t)V * d, o));
     {
         uint8_t* p;
-        E_TRY(dalloc(&p, packed_bytes(V, d, e->fmt_emb), o));
+        E_TRY(dalloc(&p, packed_bytes_tc(V, d, e->fmt_emb), o));
         e->emb_packed = p;
     }
     E_TRY(dalloc(&e->attn_norm, (size_t)L * d, o));
@@ -415,8 +419,8 @@ pf_status pf_engine_create(const pf_model_config* c, int32_t max_seqs, int32_t m
     e->mtp_set.assign(e->K, false);
     for (int h = 0; h < e->K; h++) {
         uint8_t* p;
-        E_TRY(dalloc(&p, packed_bytes(2 * d, d, WF_Q4), o)); e->mtp_gu[h] = p;
-        E_TRY(dalloc(&p, packed_bytes(d, d, WF_Q4), o)); e->mtp_down[h] = p;
+        E_TRY(dalloc(&p, packed_bytes_tc(2 * d, d, WF_Q4), o)); e->mtp_gu[h] = p;
+        E_TRY(dalloc(&p, packed_bytes_tc(d, d, WF_Q4), o)); e->mtp_down[h] = p;
         E_TRY(dalloc(&e->mtp_gu_s[h], 2 * d, o));
         E_TRY(dalloc(&e->mtp_down_s[h], d, o));
     }
@@ -568,7 +572,7 @@ static pf_status pack_host(pf_engine* e, const int8_t* w, int rows, int cols, in
     PF_CUDA(cudaMallocAsync(&tmp, (size_t)rows * cols, e->st));
     pf_status s = PF_OK;
     if (cudaMemcpyAsync(tmp, w, (size_t)rows * cols, cudaMemcpyHostToDevice, e->st) != cudaSuccess) s = PF_ERR_CUDA;
-    if (s == PF_OK) s = pack_weights(tmp, rows, cols, wf, dst, e->st);
+    if (s == PF_OK) s = pack_weights_tc(tmp, rows, cols, wf, dst, e->st);
     cudaFreeAsync(tmp, e->st);
     if (s == PF_OK && cudaStreamSynchronize(e->st) != cudaSuccess) s = PF_ERR_CUDA;
     if (s != PF_OK) return s;

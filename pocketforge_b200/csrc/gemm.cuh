@@ -40,9 +40,10 @@ struct GemmParams {
     const float* rope_sin = nullptr;
     const int* row_pos = nullptr;     // [M]
     int rope_cols = 0, head_dim = 64;
-    int splits = 1;
+    int splits = 1;          // gemm_tc_launch: 0 = choose automatically
     int32_t* ws = nullptr;  // split-K workspace, zero on entry, left zero on exit
     int* counters = nullptr;
+    size_t ws_elems = 0, cnt_elems = 0;  // capacities of ws / counters
 };
 
 // Scratch needed by a split-K launch (bytes of int32 workspace, counters).

@@ -1,0 +1,601 @@
+// gemm_tc.cu — the projection GEMM on the 5th-generation tensor cores:
+// int8 activations x packed Q4 / Q2 / int8 weights -> int32 in TMEM
+// (tcgen05.mma.kind::i8), with the epilogues of gemm.cuh.
+//
+// One CTA computes a 128-row x BN-column output tile (optionally one split
+// of K).  Per 128-wide K stage:
+//   warp 0, one thread: TMA loads of the activation tile(s) (128 x 128 B,
+//     128-byte swizzle) and of the packed weight block (BN rows x RB bytes)
+//     into the stage's buffers, completing on full_raw[s];
+//   warps 2..5: unpack the weight block to int8 in shared memory in the
+//     tensor core's K-major 128-byte-swizzled layout (the layout the TMA
+//     produces for A), fence the generic->async proxy, arrive on full_b[s];
+//   warp 1, one thread: four tcgen05.mma (K = 32 each) per activation plane
+//     into TMEM, then tcgen05.commit -> empty[s] frees the stage.
+// After the last stage a commit on `done` releases warps 2..5 to read the
+// accumulators (tcgen05.ld 32x32b: warp w reads TMEM lanes 32*(w%4)..+31,
+// i.e. output rows) and run the epilogue.  Split-K partial sums go to an
+// int32 workspace with atomics; the CTA that retires a tile last applies the
+// epilogue and re-zeroes the workspace.  No multicast loads are used.
+//
+// Every mbarrier wait is bounded (about one second of spinning); a timeout
+// latches ERR_TIMEOUT in the device error flag and the CTA drains and frees
+// its TMEM instead of hanging.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "gemm.cuh"
+#include "gemm_tc.cuh"
+
+namespace pf {
+
+namespace {
+
+constexpr int BM = 128, BK = 128;
+constexpr int NUM_THREADS = 192;  // 6 warps
+constexpr uint32_t ERR_TIMEOUT = 16u;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait: false when ~1 s passed without the phase completing.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t i = 0;; i++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 1023u) == 1023u && globaltimer() - t0 > 1000000000ull) return false;
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+    // K-major, 128-byte swizzle: 8-row groups 1024 B apart (SBO), LBO unused,
+    // version 1 (sm_100), layout type 2 (SWIZZLE_128B).
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) |
+           ((uint64_t)2 << 61);
+}
+__host__ __device__ constexpr uint32_t idesc_i8(int n) {
+    // D s32 (2 << 4), A s8 (1 << 7), B s8 (1 << 10), K-major A and B,
+    // N >> 3 at bit 17, M >> 4 at bit 24 (M = 128).
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t sext4(uint32_t y) { return y | ((y & 0x08080808u) * 0x1Eu); }
+__device__ __forceinline__ uint32_t sext2(uint32_t y) { return y | ((y & 0x02020202u) * 0x7Eu); }
+
+// Packed bytes per (row, 128-wide K block) of each format.
+template <int WF>
+__host__ __device__ constexpr int row_bytes() {
+    return WF == WF_Q4 ? 64 : (WF == WF_Q2 ? 32 : 128);
+}
+
+template <int BN, int P, int WF>
+struct Layout {
+    static constexpr int A_BYTES = BM * BK;             // one plane
+    static constexpr int RAW_BYTES = BN * row_bytes<WF>();
+    static constexpr int B_BYTES = BN * BK;
+    static constexpr int STAGE_BYTES = P * A_BYTES + B_BYTES + ((RAW_BYTES + 1023) / 1024) * 1024;
+    static constexpr int STAGES_MAX = (P == 1) ? 4 : 3;
+    static constexpr int BUDGET = 220 * 1024;
+    static constexpr int STAGES = (STAGES_MAX * STAGE_BYTES <= BUDGET) ? STAGES_MAX : (BUDGET / STAGE_BYTES);
+    static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+    static constexpr int SMEM = BAR_OFF + 256 + 1024;   // + barriers + alignment slack
+    static constexpr int TMEM_COLS = (P * BN <= 32) ? 32 : (P * BN <= 64) ? 64 : (P * BN <= 128) ? 128
+                                    : (P * BN <= 256) ? 256 : 512;
+};
+
+// Epilogue for the adjacent column pair (n, n+1) of row m (same forms as gemm.cu).
+__device__ __forceinline__ float vscale(const GemmParams& p, int32_t acc, int m, int n) {
+    const float ws = p.w_scale ? p.w_scale[n] : 1.0f;
+    return __fmul_rn(__fmul_rn(__int2float_rn(acc), p.a_scale[m]), ws);
+}
+template <int P>
+__device__ __forceinline__ float comb3(const int32_t (&a)[P]) {
+    if constexpr (P == 3) {
+        const float r = 1.0f / 254.0f;
+        return (float)a[0] + ((float)a[1] + (float)a[2] * r) * r;
+    } else {
+        return (float)a[0];
+    }
+}
+template <int P, int EPI>
+__device__ __forceinline__ void epi_pair(const GemmParams& p, int m, int n, const int32_t (&a)[P], const int32_t (&b)[P]) {
+    if constexpr (EPI == EPI_I32) {
+        *reinterpret_cast<int2*>(p.out_i32 + (size_t)m * p.ldo + n) = make_int2(a[0], b[0]);
+    } else if constexpr (EPI == EPI_F32) {
+        *reinterpret_cast<float2*>(p.out + (size_t)m * p.ldo + n) =
+            make_float2(vscale(p, a[0], m, n), vscale(p, b[0], m, n + 1));
+    } else if constexpr (EPI == EPI_QKV) {
+        float x0 = vscale(p, a[0], m, n), x1 = vscale(p, b[0], m, n + 1);
+        if (n < p.rope_cols) {  // adjacent-pair rotation (src/engine.cpp:737-748)
+            const int i2 = (n % p.head_dim) >> 1;
+            const size_t o = (size_t)p.row_pos[m] * (p.head_dim >> 1) + i2;
+            const float c = p.rope_cos[o], s = p.rope_sin[o];
+            const float r0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+            const float r1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+            x0 = r0;
+            x1 = r1;
+        }
+        *reinterpret_cast<float2*>(p.out + (size_t)m * p.ldo + n) = make_float2(x0, x1);
+    } else if constexpr (EPI == EPI_RESID) {
+        if (p.row_skip && p.row_skip[m]) return;
+        float2* r = reinterpret_cast<float2*>(p.resid + (size_t)m * p.ldo + n);
+        float2 x = *r;
+        x.x = __fadd_rn(x.x, vscale(p, a[0], m, n));
+        x.y = __fadd_rn(x.y, vscale(p, b[0], m, n + 1));
+        *r = x;
+    } else if constexpr (EPI == EPI_SWIGLU) {
+        const float g = vscale(p, a[0], m, n), u = vscale(p, b[0], m, n + 1);
+        const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
+        p.out[(size_t)m * p.ldo + (n >> 1)] = __fmul_rn(__fmul_rn(g, sig), u);
+    } else if constexpr (EPI == EPI_LOGITS3) {
+        const float s = p.a_scale[m] * p.w_scale_all;
+        *reinterpret_cast<float2*>(p.out + (size_t)m * p.ldo + n) = make_float2(comb3<P>(a) * s, comb3<P>(b) * s);
+    } else if constexpr (EPI == EPI_MTP_SWIGLU3) {
+        const float g = comb3<P>(a) * p.a_scale[m] * p.w_scale[n];
+        const float u = comb3<P>(b) * p.a_scale[m] * p.w_scale[n + 1];
+        p.out[(size_t)m * p.ldo + (n >> 1)] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+    } else if constexpr (EPI == EPI_MTP_RESID3) {
+        float2* r = reinterpret_cast<float2*>(p.resid + (size_t)m * p.ldo + n);
+        float2 x = *r;
+        x.x = __fadd_rn(x.x, comb3<P>(a) * p.a_scale[m] * p.w_scale[n]);
+        x.y = __fadd_rn(x.y, comb3<P>(b) * p.a_scale[m] * p.w_scale[n + 1]);
+        *r = x;
+    }
+}
+
+template <int BN, int P, int WF, int EPI>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmParams p,
+                   int plane_rows, uint32_t* err) {
+    using Ly = Layout<BN, P, WF>;
+    constexpr int STAGES = Ly::STAGES;
+    constexpr int RB = row_bytes<WF>();
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t bars = sbase + Ly::BAR_OFF;
+    auto full_raw = [&](int s) { return bars + 8u * s; };
+    auto full_b = [&](int s) { return bars + 8u * (STAGES + s); };
+    auto empty = [&](int s) { return bars + 8u * (2 * STAGES + s); };
+    const uint32_t done = bars + 8u * (3 * STAGES);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Ly::BAR_OFF + 8 * (3 * STAGES + 1));
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Ly::BAR_OFF + 8 * (3 * STAGES + 1) + 8);
+    auto a_addr = [&](int s, int pl) { return sbase + (uint32_t)(s * Ly::STAGE_BYTES + pl * Ly::A_BYTES); };
+    auto b_addr = [&](int s) { return sbase + (uint32_t)(s * Ly::STAGE_BYTES + P * Ly::A_BYTES); };
+    auto raw_addr = [&](int s) { return sbase + (uint32_t)(s * Ly::STAGE_BYTES + P * Ly::A_BYTES + Ly::B_BYTES); };
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+    const int nkt = p.K / BK;
+    const int per = (nkt + p.splits - 1) / p.splits;
+    const int kt0 = blockIdx.z * per, kt1 = min(nkt, kt0 + per);
+    const int nst = max(0, kt1 - kt0);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(full_raw(s), 1);
+            mbar_init(full_b(s), 128);
+            mbar_init(empty(s), 1);
+        }
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(Ly::TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const uint32_t tmem = *tmem_slot;
+
+    auto fail = [&]() {
+        *abort_flag = 1;
+        if (err) atomicOr(err, ERR_TIMEOUT);
+    };
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            int issued = 0;
+            for (int i = 0; i < nst && !*abort_flag; i++) {
+                const int s = i % STAGES, ph = (i / STAGES) & 1;
+                if (!mbar_wait(empty(s), ph ^ 1)) {
+                    fail();
+                    break;
+                }
+                const int kt = kt0 + i;
+                mbar_expect_tx(full_raw(s), (uint32_t)(P * Ly::A_BYTES + Ly::RAW_BYTES));
+                for (int pl = 0; pl < P; pl++) tma_load_2d(a_addr(s, pl), &tmA, kt * BK, pl * plane_rows + m0, full_raw(s));
+                tma_load_2d(raw_addr(s), &tmB, 0, kt * p.N + n0, full_raw(s));
+                issued = i + 1;
+            }
+            if (*abort_flag) {
+                // Let this CTA's copies still in flight land (bounded) before its
+                // shared memory is released.
+                for (int j = max(0, issued - STAGES); j < issued; j++)
+                    (void)mbar_wait(full_raw(j % STAGES), (j / STAGES) & 1);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_i8(BN);
+            for (int i = 0; i < nst && !*abort_flag; i++) {
+                const int s = i % STAGES, ph = (i / STAGES) & 1;
+                if (!mbar_wait(full_raw(s), ph) || !mbar_wait(full_b(s), ph)) {
+                    fail();
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;");
+                const uint64_t bd = sw128_desc(b_addr(s));
+#pragma unroll
+                for (int pl = 0; pl < P; pl++) {
+                    const uint64_t ad = sw128_desc(a_addr(s, pl));
+#pragma unroll
+                    for (int kk = 0; kk < BK / 32; kk++)  // K = 32 bytes per MMA: +2 in 16-byte units
+                        umma_i8(tmem + (uint32_t)(pl * BN), ad + 2 * kk, bd + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                }
+                umma_commit(empty(s));
+            }
+            umma_commit(done);  // fires once every issued MMA has completed
+        }
+    } else {
+        // ---------------- weight unpack (warps 2..5), then epilogue ----------------
+        const int t = threadIdx.x - 64;  // 0..127
+        constexpr int CH_IN = BN * RB / 16;  // 16-byte packed chunks per stage
+        for (int i = 0; i < nst && !*abort_flag; i++) {
+            const int s = i % STAGES, ph = (i / STAGES) & 1;
+            if (!mbar_wait(full_raw(s), ph)) {
+                fail();
+                break;
+            }
+            const uint8_t* raw = smem + (raw_addr(s) - sbase);
+            uint8_t* bt = smem + (b_addr(s) - sbase);
+            for (int q = t; q < CH_IN; q += 128) {
+                const int row = q / (RB / 16), c = q % (RB / 16);
+                const uint4 w = *reinterpret_cast<const uint4*>(raw + (size_t)q * 16);
+                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+                const int r7 = row & 7;
+                uint8_t* rb = bt + (row >> 3) * 1024 + r7 * 128;
+                if constexpr (WF == WF_Q4) {
+                    uint4 lo, hi;  // k [32c, 32c+16) and [32c+16, 32c+32)
+                    lo.x = sext4(ws[0] & 0x0F0F0F0Fu); hi.x = sext4((ws[0] >> 4) & 0x0F0F0F0Fu);
+                    lo.y = sext4(ws[1] & 0x0F0F0F0Fu); hi.y = sext4((ws[1] >> 4) & 0x0F0F0F0Fu);
+                    lo.z = sext4(ws[2] & 0x0F0F0F0Fu); hi.z = sext4((ws[2] >> 4) & 0x0F0F0F0Fu);
+                    lo.w = sext4(ws[3] & 0x0F0F0F0Fu); hi.w = sext4((ws[3] >> 4) & 0x0F0F0F0Fu);
+                    *reinterpret_cast<uint4*>(rb + (((2 * c) ^ r7) << 4)) = lo;
+                    *reinterpret_cast<uint4*>(rb + (((2 * c + 1) ^ r7) << 4)) = hi;
+                } else if constexpr (WF == WF_Q2) {
+#pragma unroll
+                    for (int sft = 0; sft < 4; sft++) {  // k [64c + 16 sft, +16)
+                        uint4 o;
+                        o.x = sext2((ws[0] >> (2 * sft)) & 0x03030303u);
+                        o.y = sext2((ws[1] >> (2 * sft)) & 0x03030303u);
+                        o.z = sext2((ws[2] >> (2 * sft)) & 0x03030303u);
+                        o.w = sext2((ws[3] >> (2 * sft)) & 0x03030303u);
+                        *reinterpret_cast<uint4*>(rb + (((4 * c + sft) ^ r7) << 4)) = o;
+                    }
+                } else {
+                    *reinterpret_cast<uint4*>(rb + ((c ^ r7) << 4)) = w;
+                }
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive(full_b(s));
+        }
+        // ---------------- epilogue ----------------
+        // `ok` must be the same for all 128 epilogue threads: the TMEM loads
+        // below are warp-collective and the split-K path uses a named barrier.
+        __shared__ int s_ok, s_last;
+        const bool okl = !*abort_flag && mbar_wait(done, 0);
+        if (!okl) fail();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (t == 0) s_ok = !*abort_flag;
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        const bool ok = s_ok != 0;
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        const int sub = warp & 3;                 // TMEM lanes 32*sub .. 32*sub+31 = tile rows
+        const int m = m0 + sub * 32 + lane;
+        const int m_act = p.m_dev ? min(p.M, *p.m_dev) : p.M;
+        const bool row_ok = m < m_act;
+        const uint32_t tbase = tmem + ((uint32_t)(sub * 32) << 16);
+        if (ok && nst > 0) {
+            for (int j = 0; j < BN / 16; j++) {
+                uint32_t r[P][16];
+#pragma unroll
+                for (int pl = 0; pl < P; pl++) tmem_ld16(tbase + (uint32_t)(pl * BN + j * 16), r[pl]);
+                if (!row_ok) continue;
+                if (p.splits > 1) {
+#pragma unroll
+                    for (int pl = 0; pl < P; pl++)
+#pragma unroll
+                        for (int c = 0; c < 16; c++)
+                            if (r[pl][c] != 0)
+                                atomicAdd(p.ws + ((size_t)pl * p.M + m) * p.N + n0 + j * 16 + c, (int32_t)r[pl][c]);
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 16; c += 2) {
+                        int32_t a[P], b[P];
+#pragma unroll
+                        for (int pl = 0; pl < P; pl++) {
+                            a[pl] = (int32_t)r[pl][c];
+                            b[pl] = (int32_t)r[pl][c + 1];
+                        }
+                        epi_pair<P, EPI>(p, m, n0 + j * 16 + c, a, b);
+                    }
+                }
+            }
+        }
+        if (p.splits > 1 && ok) {
+            // The split that retires the tile last applies the epilogue.
+            __threadfence();
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+            if (t == 0) s_last = (atomicAdd(p.counters + tile, 1) == p.splits - 1);
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (s_last) {
+                __threadfence();
+                if (row_ok) {
+                    for (int nn = 0; nn < BN; nn += 2) {
+                        int32_t a[P], b[P];
+#pragma unroll
+                        for (int pl = 0; pl < P; pl++) {
+                            a[pl] = atomicExch(p.ws + ((size_t)pl * p.M + m) * p.N + n0 + nn, 0);
+                            b[pl] = atomicExch(p.ws + ((size_t)pl * p.M + m) * p.N + n0 + nn + 1, 0);
+                        }
+                        epi_pair<P, EPI>(p, m, n0 + nn, a, b);
+                    }
+                }
+                if (t == 0) p.counters[tile] = 0;
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Ly::TMEM_COLS));
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host side: tensor maps through the driver entry point (no libcuda link).
+// ---------------------------------------------------------------------------
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+pf_status get_encode(EncodeTiled* fn) {
+    static std::mutex mu;
+    static EncodeTiled cached = nullptr;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!cached) {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        PF_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q));
+        PF_CHECK(f && q == cudaDriverEntryPointSuccess, "cuTensorMapEncodeTiled unavailable");
+        cached = reinterpret_cast<EncodeTiled>(f);
+    }
+    *fn = cached;
+    return PF_OK;
+}
+
+pf_status make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t row_stride,
+                   uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz) {
+    EncodeTiled enc;
+    PF_TRY(get_encode(&enc));
+    const cuuint64_t dims[2] = {inner, rows};
+    const cuuint64_t strides[1] = {row_stride};
+    const cuuint32_t box[2] = {box_inner, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    PF_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return PF_OK;
+}
+
+template <int BN, int P, int WF, int EPI>
+pf_status launch_tc(const GemmParams& p, int plane_rows, cudaStream_t st) {
+    using Ly = Layout<BN, P, WF>;
+    static_assert(Ly::STAGES >= 2, "shared memory budget too small");
+    CUtensorMap ta, tb;
+    const uint64_t a_rows = (P == 1) ? (uint64_t)p.M : (uint64_t)P * plane_rows;
+    PF_TRY(make_map(&ta, p.A, (uint64_t)p.K, a_rows, (uint64_t)p.lda, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B));
+    PF_TRY(make_map(&tb, p.W, (uint64_t)row_bytes<WF>(), (uint64_t)(p.K / BK) * p.N, (uint64_t)row_bytes<WF>(),
+                    row_bytes<WF>(), BN, CU_TENSOR_MAP_SWIZZLE_NONE));
+    static bool attr = false;
+    if (!attr) {
+        PF_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, P, WF, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Ly::SMEM));
+        attr = true;
+    }
+    dim3 grid(p.N / BN, ceil_div(p.M, BM), p.splits);
+    gemm_tc_kernel<BN, P, WF, EPI><<<grid, NUM_THREADS, Ly::SMEM, st>>>(ta, tb, p, plane_rows, device_error_flag());
+    return launch_check("gemm_tc");
+}
+
+template <int BN, int P, int EPI>
+pf_status launch_wf(const GemmParams& p, int plane_rows, cudaStream_t st) {
+    switch (p.wf) {
+        case WF_Q4: return launch_tc<BN, P, WF_Q4, EPI>(p, plane_rows, st);
+        case WF_Q2: return launch_tc<BN, P, WF_Q2, EPI>(p, plane_rows, st);
+        default: return launch_tc<BN, P, WF_I8, EPI>(p, plane_rows, st);
+    }
+}
+
+template <int BN>
+pf_status launch_bn(const GemmParams& p, int planes, int plane_rows, cudaStream_t st) {
+    if (planes == 3) {
+        switch (p.epi) {
+            case EPI_LOGITS3: return launch_wf<BN, 3, EPI_LOGITS3>(p, plane_rows, st);
+            case EPI_MTP_SWIGLU3: return launch_wf<BN, 3, EPI_MTP_SWIGLU3>(p, plane_rows, st);
+            default: return launch_wf<BN, 3, EPI_MTP_RESID3>(p, plane_rows, st);
+        }
+    }
+    switch (p.epi) {
+        case EPI_I32: return launch_wf<BN, 1, EPI_I32>(p, plane_rows, st);
+        case EPI_F32: return launch_wf<BN, 1, EPI_F32>(p, plane_rows, st);
+        case EPI_QKV: return launch_wf<BN, 1, EPI_QKV>(p, plane_rows, st);
+        case EPI_RESID: return launch_wf<BN, 1, EPI_RESID>(p, plane_rows, st);
+        default: return launch_wf<BN, 1, EPI_SWIGLU>(p, plane_rows, st);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Packing to the tensor-core layout: [K/128][N][RB] with, per 128-wide block,
+//   Q4: 4 chunks of 16 B; chunk c byte j = low nibble k 32c+j, high nibble k 32c+16+j;
+//   Q2: 2 chunks of 16 B; chunk c byte j bits [2s, 2s+2) = k 64c+16s+j;
+//   I8: the 128 bytes in order.  Fields are two's complement (v & 0xF, v & 0x3).
+// ---------------------------------------------------------------------------
+__global__ void pack_tc_kernel(const int8_t* __restrict__ w, int rows, int cols, int wf, uint8_t* __restrict__ out,
+                               int nkb, uint32_t* err) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // one 16-byte chunk
+    const int rb = wf == WF_Q4 ? 64 : (wf == WF_Q2 ? 32 : 128);
+    const int cpr = rb / 16;
+    const int64_t total = (int64_t)nkb * rows * cpr;
+    if (idx >= total) return;
+    const int c = (int)(idx % cpr);
+    const int64_t rem = idx / cpr;
+    const int n = (int)(rem % rows);
+    const int kb = (int)(rem / rows);
+    auto val = [&](int k) -> int { return k < cols ? (int)w[(size_t)n * cols + k] : 0; };
+    uint8_t bytes[16];
+    bool bad = false;
+    for (int j = 0; j < 16; j++) {
+        const int k0 = kb * 128;
+        if (wf == WF_Q4) {
+            const int lo = val(k0 + 32 * c + j), hi = val(k0 + 32 * c + 16 + j);
+            bad |= lo < -8 || lo > 7 || hi < -8 || hi > 7;
+            bytes[j] = (uint8_t)((lo & 0xF) | ((hi & 0xF) << 4));
+        } else if (wf == WF_Q2) {
+            uint8_t b = 0;
+            for (int s = 0; s < 4; s++) {
+                const int v = val(k0 + 64 * c + 16 * s + j);
+                bad |= v < -2 || v > 1;
+                b |= (uint8_t)((v & 3) << (2 * s));
+            }
+            bytes[j] = b;
+        } else {
+            bytes[j] = (uint8_t)(val(k0 + 16 * c + j) & 0xFF);
+        }
+    }
+    uint4 o;
+    memcpy(&o, bytes, 16);
+    reinterpret_cast<uint4*>(out)[idx] = o;
+    if (bad) atomicOr(err, ERR_WEIGHT_RANGE);
+}
+
+}  // namespace
+
+size_t packed_bytes_tc(int rows, int cols, int wf) {
+    const int rb = wf == WF_Q4 ? 64 : (wf == WF_Q2 ? 32 : 128);
+    return (size_t)ceil_div(cols, 128) * rows * rb;
+}
+
+pf_status pack_weights_tc(const int8_t* w, int rows, int cols, int wf, void* packed, cudaStream_t st) {
+    PF_CHECK(rows > 0 && cols > 0 && w && packed, "pack_weights_tc: bad arguments");
+    const int nkb = ceil_div(cols, 128);
+    const int cpr = (wf == WF_Q4 ? 64 : (wf == WF_Q2 ? 32 : 128)) / 16;
+    const int64_t total = (int64_t)nkb * rows * cpr;
+    pack_tc_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(w, rows, cols, wf, (uint8_t*)packed, nkb,
+                                                                     device_error_flag());
+    return launch_check("pack_weights_tc");
+}
+
+int gemm_tc_pick_bn(int M, int N) {
+    if (N % 128 != 0) return 64;
+    const int tiles128 = ceil_div(M, BM) * (N / 128);
+    return tiles128 >= 148 ? 128 : 64;
+}
+
+int gemm_tc_pick_splits(int M, int N, int K, int bn, bool have_ws) {
+    if (!have_ws) return 1;
+    const int tiles = ceil_div(M, BM) * (N / bn);
+    const int nkt = K / BK;
+    int s = (tiles >= 120) ? 1 : ceil_div(148, tiles);
+    s = std::min(s, std::max(1, nkt / 2));
+    return std::max(1, std::min(s, 8));
+}
+
+pf_status gemm_tc_launch(const GemmParams& p0, int planes, int plane_rows, cudaStream_t st) {
+    GemmParams p = p0;
+    PF_CHECK(p.M > 0 && p.N > 0 && p.K > 0, "gemm_tc: empty shape");
+    PF_CHECK(p.N % 64 == 0, "gemm_tc: N=%d must be a multiple of 64", p.N);
+    PF_CHECK(p.K % BK == 0, "gemm_tc: K=%d must be a multiple of %d", p.K, BK);
+    PF_CHECK(p.lda % 16 == 0 && p.lda >= p.K, "gemm_tc: lda=%d must be >= K and a multiple of 16", p.lda);
+    PF_CHECK((reinterpret_cast<uintptr_t>(p.A) & 15) == 0 && (reinterpret_cast<uintptr_t>(p.W) & 15) == 0,
+             "gemm_tc: operands must be 16-byte aligned");
+    PF_CHECK(planes == 1 || planes == 3, "gemm_tc: planes must be 1 or 3");
+    PF_CHECK(planes == 1 || (plane_rows >= p.M && p.plane_stride == (int64_t)plane_rows * p.lda),
+             "gemm_tc: plane layout must be [planes][plane_rows][lda]");
+    const bool three = p.epi == EPI_LOGITS3 || p.epi == EPI_MTP_SWIGLU3 || p.epi == EPI_MTP_RESID3;
+    PF_CHECK(three == (planes == 3), "gemm_tc: epilogue %d does not take %d planes", p.epi, planes);
+    const int bn = gemm_tc_pick_bn(p.M, p.N);
+    if (p.splits <= 0) {  // automatic: split K only when the tiles do not fill the GPU and a workspace fits
+        p.splits = gemm_tc_pick_splits(p.M, p.N, p.K, bn, p.ws != nullptr && p.counters != nullptr);
+        const size_t tiles = (size_t)ceil_div(p.M, BM) * (p.N / bn);
+        if (p.splits > 1 && ((size_t)planes * p.M * p.N > p.ws_elems || tiles > p.cnt_elems)) p.splits = 1;
+    }
+    PF_CHECK(p.splits == 1 || (p.ws && p.counters), "gemm_tc: split-K needs a workspace");
+    PF_CHECK(p.splits <= p.K / BK, "gemm_tc: more splits than K blocks");
+    if (bn == 128) return launch_bn<128>(p, planes, plane_rows, st);
+    return launch_bn<64>(p, planes, plane_rows, st);
+}
+
+}  // namespace pf

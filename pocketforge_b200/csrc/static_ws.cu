@@ -21,6 +21,7 @@
 #include <mutex>
 
 #include "gemm.cuh"
+#include "gemm_tc.cuh"
 
 namespace pf {
 namespace {
@@ -74,9 +75,9 @@ extern "C" pf_status pf_gemm_packed_static(const int8_t* Aq, const float* a_scal
     PF_CHECK((size_t)M * (size_t)N <= kStaticWsElems,
              "pf_gemm_packed_static: M*N = %lld exceeds the static workspace of %zu partial sums",
              (long long)M * N, kStaticWsElems);
-    PF_CHECK(gemm_counter_count(M, N) <= (size_t)kStaticCounters,
-             "pf_gemm_packed_static: %zu output tiles exceed the %d static tile counters", gemm_counter_count(M, N),
-             kStaticCounters);
+    const size_t tiles = (size_t)ceil_div(M, 128) * (size_t)ceil_div(N, 64);
+    PF_CHECK(tiles <= (size_t)kStaticCounters, "pf_gemm_packed_static: %zu output tiles exceed the %d static tile counters",
+             tiles, kStaticCounters);
     StaticAddr a;
     PF_TRY(static_addr(&a));
     cudaStream_t st = as_stream(stream);
@@ -84,13 +85,15 @@ extern "C" pf_status pf_gemm_packed_static(const int8_t* Aq, const float* a_scal
     p.A = Aq; p.lda = K; p.a_scale = a_scale; p.M = M; p.N = N; p.K = K;
     p.W = packed_w; p.wf = wfmt_of_qtype(qtype); p.w_scale = w_scale;
     p.epi = EPI_F32; p.out = C; p.ldo = N;
-    p.splits = std::max(2, gemm_pick_splits(M, N, K, true));
-    if (K / 128 < 2) p.splits = 1;
+    const int bn = gemm_tc_pick_bn(M, N);
+    p.splits = std::min(K / 128, std::max(2, gemm_tc_pick_splits(M, N, K, bn, true)));
     p.ws = a.ws;
     p.counters = a.cnt;
+    p.ws_elems = kStaticWsElems;
+    p.cnt_elems = kStaticCounters;
     // The kernel leaves the workspace zeroed, but an earlier call that did not
     // complete may not have: clear what this call reads before its first use.
     PF_CUDA(cudaMemsetAsync(a.ws, 0, (size_t)M * N * sizeof(int32_t), st));
-    PF_CUDA(cudaMemsetAsync(a.cnt, 0, gemm_counter_count(M, N) * sizeof(int), st));
-    return gemm_launch(p, 1, st);
+    PF_CUDA(cudaMemsetAsync(a.cnt, 0, tiles * sizeof(int), st));
+    return gemm_tc_launch(p, 1, M, st);
 }

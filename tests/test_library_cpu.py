@@ -44,7 +44,7 @@ def test_packed_sizes():
     assert L.pf_packed_weight_bytes(2048, 5632, 2) == 2048 * 5632 // 4
     assert L.pf_packed_weight_bytes(2048, 5632, 3) == 2048 * 5632 // 4
     assert L.pf_packed_weight_bytes(64, 128, 0) == 64 * 128
-    assert L.pf_packed_weight_bytes(3, 5, 1) == 8 * 128 // 2  # one padded group
+    assert L.pf_packed_weight_bytes(3, 5, 1) == 3 * 64  # K padded to one 128-wide block
 
 
 @pytest.mark.parametrize("qtype,rows,cols", [(1, 64, 128), (2, 40, 96), (3, 32, 64), (0, 16, 64), (1, 7, 33)])
