@@ -127,72 +127,131 @@ struct Layout {
     static constexpr int RAW_BYTES = BN * row_bytes<WF>();
     static constexpr int B_BYTES = BN * BK;
     static constexpr int STAGE_BYTES = P * A_BYTES + B_BYTES + ((RAW_BYTES + 1023) / 1024) * 1024;
-    static constexpr int STAGES_MAX = (P == 1) ? 4 : 3;
+    static constexpr int STAGES_MAX = (P == 1) ? 8 : 3;
     static constexpr int BUDGET = 220 * 1024;
     static constexpr int STAGES = (STAGES_MAX * STAGE_BYTES <= BUDGET) ? STAGES_MAX : (BUDGET / STAGE_BYTES);
     static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
-    static constexpr int SMEM = BAR_OFF + 256 + 1024;   // + barriers + alignment slack
+    static constexpr int WSC_OFF = BAR_OFF + 256;        // BN column scales (fp32)
+    static constexpr int SMEM = WSC_OFF + BN * 4 + 1024;  // + alignment slack
+    // Epilogue staging (reuses the stage ring): 4 warps x 32 rows x (BN + 4) fp32.
+    static constexpr int SROW = BN + 4;
+    static_assert(4 * 32 * SROW * 4 <= STAGES * STAGE_BYTES, "staging does not fit the stage ring");
     static constexpr int TMEM_COLS = (P * BN <= 32) ? 32 : (P * BN <= 64) ? 64 : (P * BN <= 128) ? 128
                                     : (P * BN <= 256) ? 256 : 512;
 };
 
-// Epilogue for the adjacent column pair (n, n+1) of row m (same forms as gemm.cu).
-__device__ __forceinline__ float vscale(const GemmParams& p, int32_t acc, int m, int n) {
-    const float ws = p.w_scale ? p.w_scale[n] : 1.0f;
-    return __fmul_rn(__fmul_rn(__int2float_rn(acc), p.a_scale[m]), ws);
-}
 template <int P>
 __device__ __forceinline__ float comb3(const int32_t (&a)[P]) {
     if constexpr (P == 3) {
         const float r = 1.0f / 254.0f;
-        return (float)a[0] + ((float)a[1] + (float)a[2] * r) * r;
+        return __fadd_rn(__int2float_rn(a[0]),
+                         __fmul_rn(__fadd_rn(__int2float_rn(a[1]), __fmul_rn(__int2float_rn(a[2]), r)), r));
     } else {
-        return (float)a[0];
+        return __int2float_rn(a[0]);
     }
 }
+// Value of one output column of row m before the column-pair step:
+// v = ((float)acc * a_scale[m]) * w_scale[n] (matmul_quantized's two
+// roundings, src/matmul_neon.cpp:176-180), comb * (a_scale[m] * w_scale_all)
+// for the tied unembedding, comb * a_scale[m] * w_scale[n] for the MTP forms,
+// or the raw int32 bits for EPI_I32.
 template <int P, int EPI>
-__device__ __forceinline__ void epi_pair(const GemmParams& p, int m, int n, const int32_t (&a)[P], const int32_t (&b)[P]) {
+__device__ __forceinline__ float col_value(const int32_t (&a)[P], float a_s, float w_s, float s_all) {
     if constexpr (EPI == EPI_I32) {
-        *reinterpret_cast<int2*>(p.out_i32 + (size_t)m * p.ldo + n) = make_int2(a[0], b[0]);
-    } else if constexpr (EPI == EPI_F32) {
-        *reinterpret_cast<float2*>(p.out + (size_t)m * p.ldo + n) =
-            make_float2(vscale(p, a[0], m, n), vscale(p, b[0], m, n + 1));
-    } else if constexpr (EPI == EPI_QKV) {
-        float x0 = vscale(p, a[0], m, n), x1 = vscale(p, b[0], m, n + 1);
-        if (n < p.rope_cols) {  // adjacent-pair rotation (src/engine.cpp:737-748)
-            const int i2 = (n % p.head_dim) >> 1;
-            const size_t o = (size_t)p.row_pos[m] * (p.head_dim >> 1) + i2;
-            const float c = p.rope_cos[o], s = p.rope_sin[o];
-            const float r0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-            const float r1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-            x0 = r0;
-            x1 = r1;
-        }
-        *reinterpret_cast<float2*>(p.out + (size_t)m * p.ldo + n) = make_float2(x0, x1);
-    } else if constexpr (EPI == EPI_RESID) {
-        if (p.row_skip && p.row_skip[m]) return;
-        float2* r = reinterpret_cast<float2*>(p.resid + (size_t)m * p.ldo + n);
-        float2 x = *r;
-        x.x = __fadd_rn(x.x, vscale(p, a[0], m, n));
-        x.y = __fadd_rn(x.y, vscale(p, b[0], m, n + 1));
-        *r = x;
-    } else if constexpr (EPI == EPI_SWIGLU) {
-        const float g = vscale(p, a[0], m, n), u = vscale(p, b[0], m, n + 1);
-        const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
-        p.out[(size_t)m * p.ldo + (n >> 1)] = __fmul_rn(__fmul_rn(g, sig), u);
+        return __int_as_float(a[0]);
     } else if constexpr (EPI == EPI_LOGITS3) {
-        const float s = p.a_scale[m] * p.w_scale_all;
-        *reinterpret_cast<float2*>(p.out + (size_t)m * p.ldo + n) = make_float2(comb3<P>(a) * s, comb3<P>(b) * s);
-    } else if constexpr (EPI == EPI_MTP_SWIGLU3) {
-        const float g = comb3<P>(a) * p.a_scale[m] * p.w_scale[n];
-        const float u = comb3<P>(b) * p.a_scale[m] * p.w_scale[n + 1];
-        p.out[(size_t)m * p.ldo + (n >> 1)] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
-    } else if constexpr (EPI == EPI_MTP_RESID3) {
-        float2* r = reinterpret_cast<float2*>(p.resid + (size_t)m * p.ldo + n);
-        float2 x = *r;
-        x.x = __fadd_rn(x.x, comb3<P>(a) * p.a_scale[m] * p.w_scale[n]);
-        x.y = __fadd_rn(x.y, comb3<P>(b) * p.a_scale[m] * p.w_scale[n + 1]);
-        *r = x;
+        return __fmul_rn(comb3<P>(a), s_all);
+    } else if constexpr (EPI == EPI_MTP_SWIGLU3 || EPI == EPI_MTP_RESID3) {
+        return __fmul_rn(__fmul_rn(comb3<P>(a), a_s), w_s);
+    } else {
+        return __fmul_rn(__fmul_rn(__int2float_rn(a[0]), a_s), w_s);
+    }
+}
+
+__device__ __forceinline__ float engine_swiglu(float g, float u) {  // engine FFN form
+    const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
+    return __fmul_rn(__fmul_rn(g, sig), u);
+}
+__device__ __forceinline__ float mtp_swiglu(float g, float u) {  // MTP head FFN form
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+__device__ __forceinline__ void rope_pair(float& x0, float& x1, float c, float s) {
+    // adjacent-pair rotation (src/engine.cpp:737-748)
+    const float r0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+    const float r1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+    x0 = r0;
+    x1 = r1;
+}
+
+// Pass 2 of the epilogue: one warp writes its 32 staged rows.  Lane l owns
+// columns 4*(l % CPR) .. +3 of row l / CPR of each group, so every store
+// (and every residual load) is a contiguous run of a row.  Row-dependent
+// inputs (residual rows, RoPE angles) are fetched for U groups before any of
+// them is written, keeping several loads in flight.
+template <int BN, int EPI>
+__device__ __forceinline__ void store_rows(const GemmParams& p, const float* stg, int rbase, int n0, int lane) {
+    constexpr int SROW = BN + 4;
+    constexpr int CPR = BN / 4, RPI = 32 / CPR, ITERS = 32 / RPI, U = 4;
+    static_assert(ITERS % U == 0, "row groups");
+    const int cg = lane % CPR, ro = lane / CPR;
+    const int n = n0 + 4 * cg;
+    const int m_act = p.m_dev ? min(p.M, *p.m_dev) : p.M;
+    constexpr bool RESID = EPI == EPI_RESID || EPI == EPI_MTP_RESID3;
+    for (int g0 = 0; g0 < ITERS; g0 += U) {
+        int rr[U];
+        bool act[U];
+        float4 pre[U];  // residual row segment, or (cos0, sin0, cos1, sin1)
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            rr[u] = (g0 + u) * RPI + ro;
+            const int m = rbase + rr[u];
+            act[u] = m < m_act;
+            if constexpr (EPI == EPI_RESID) act[u] = act[u] && !(p.row_skip && p.row_skip[m]);
+            pre[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (!act[u]) continue;
+            if constexpr (RESID) {
+                pre[u] = *reinterpret_cast<const float4*>(p.resid + (size_t)m * p.ldo + n);
+            } else if constexpr (EPI == EPI_QKV) {
+                if (n < p.rope_cols) {
+                    const int i2 = (n % p.head_dim) >> 1;  // even: pairs i2, i2 + 1
+                    const size_t o = (size_t)p.row_pos[m] * (p.head_dim >> 1) + i2;
+                    const float2 c = *reinterpret_cast<const float2*>(p.rope_cos + o);
+                    const float2 s = *reinterpret_cast<const float2*>(p.rope_sin + o);
+                    pre[u] = make_float4(c.x, s.x, c.y, s.y);
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            if (!act[u]) continue;
+            const int m = rbase + rr[u];
+            float4 x = *reinterpret_cast<const float4*>(stg + rr[u] * SROW + 4 * cg);
+            if constexpr (EPI == EPI_I32) {
+                *reinterpret_cast<int4*>(p.out_i32 + (size_t)m * p.ldo + n) =
+                    make_int4(__float_as_int(x.x), __float_as_int(x.y), __float_as_int(x.z), __float_as_int(x.w));
+            } else if constexpr (EPI == EPI_F32 || EPI == EPI_LOGITS3) {
+                *reinterpret_cast<float4*>(p.out + (size_t)m * p.ldo + n) = x;
+            } else if constexpr (EPI == EPI_QKV) {
+                if (n < p.rope_cols) {
+                    rope_pair(x.x, x.y, pre[u].x, pre[u].y);
+                    rope_pair(x.z, x.w, pre[u].z, pre[u].w);
+                }
+                *reinterpret_cast<float4*>(p.out + (size_t)m * p.ldo + n) = x;
+            } else if constexpr (RESID) {
+                float4 r = pre[u];
+                r.x = __fadd_rn(r.x, x.x);
+                r.y = __fadd_rn(r.y, x.y);
+                r.z = __fadd_rn(r.z, x.z);
+                r.w = __fadd_rn(r.w, x.w);
+                *reinterpret_cast<float4*>(p.resid + (size_t)m * p.ldo + n) = r;
+            } else if constexpr (EPI == EPI_SWIGLU) {
+                *reinterpret_cast<float2*>(p.out + (size_t)m * p.ldo + (n >> 1)) =
+                    make_float2(engine_swiglu(x.x, x.y), engine_swiglu(x.z, x.w));
+            } else if constexpr (EPI == EPI_MTP_SWIGLU3) {
+                *reinterpret_cast<float2*>(p.out + (size_t)m * p.ldo + (n >> 1)) =
+                    make_float2(mtp_swiglu(x.x, x.y), mtp_swiglu(x.z, x.w));
+            }
+        }
     }
 }
 
@@ -226,7 +285,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
-            mbar_init(full_raw(s), 1);
+            mbar_init(full_raw(s), P + 1);  // one arrival per issuing lane
             mbar_init(full_b(s), 128);
             mbar_init(empty(s), 1);
         }
@@ -251,26 +310,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
-        if (lane == 0) {
-            int issued = 0;
-            for (int i = 0; i < nst && !*abort_flag; i++) {
-                const int s = i % STAGES, ph = (i / STAGES) & 1;
-                if (!mbar_wait(empty(s), ph ^ 1)) {
+        // Copies issued by one thread are processed one after another, so
+        // each (slot, copy) pair has its own lane: lane s*(P+1)+c issues copy
+        // c (activation plane c, or the packed weights for c == P) of every
+        // stage that uses slot s, and arrives on full_raw[s] with its bytes.
+        constexpr int COPIES = P + 1;
+        static_assert(STAGES * COPIES <= 32, "one lane per (slot, copy)");
+        if (lane < STAGES * COPIES) {
+            const int s = lane / COPIES, c = lane % COPIES;
+            const uint32_t bytes = (uint32_t)(c < P ? Ly::A_BYTES : Ly::RAW_BYTES);
+            int last = -1;
+            for (int i = s; i < nst && !*abort_flag; i += STAGES) {
+                if (!mbar_wait(empty(s), ((i / STAGES) & 1) ^ 1)) {
                     fail();
                     break;
                 }
                 const int kt = kt0 + i;
-                mbar_expect_tx(full_raw(s), (uint32_t)(P * Ly::A_BYTES + Ly::RAW_BYTES));
-                for (int pl = 0; pl < P; pl++) tma_load_2d(a_addr(s, pl), &tmA, kt * BK, pl * plane_rows + m0, full_raw(s));
-                tma_load_2d(raw_addr(s), &tmB, 0, kt * p.N + n0, full_raw(s));
-                issued = i + 1;
+                mbar_expect_tx(full_raw(s), bytes);
+                if (c < P)
+                    tma_load_2d(a_addr(s, c), &tmA, kt * BK, c * plane_rows + m0, full_raw(s));
+                else
+                    tma_load_2d(raw_addr(s), &tmB, 0, kt * p.N + n0, full_raw(s));
+                last = i;
             }
-            if (*abort_flag) {
-                // Let this CTA's copies still in flight land (bounded) before its
-                // shared memory is released.
-                for (int j = max(0, issued - STAGES); j < issued; j++)
-                    (void)mbar_wait(full_raw(j % STAGES), (j / STAGES) & 1);
-            }
+            // On abort, let this lane's copy still in flight land (bounded)
+            // before the CTA's shared memory is released.
+            if (*abort_flag && last >= 0) (void)mbar_wait(full_raw(s), (last / STAGES) & 1);
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
@@ -298,7 +363,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     } else {
         // ---------------- weight unpack (warps 2..5), then epilogue ----------------
         const int t = threadIdx.x - 64;  // 0..127
+        float* s_wsc = reinterpret_cast<float*>(smem + Ly::WSC_OFF);
+        for (int c = t; c < BN; c += 128) s_wsc[c] = p.w_scale ? p.w_scale[n0 + c] : 1.0f;
         constexpr int CH_IN = BN * RB / 16;  // 16-byte packed chunks per stage
+        static_assert(CH_IN % 128 == 0, "unpack assumes whole rounds of 128 chunks");
+        constexpr int PER = CH_IN / 128;
         for (int i = 0; i < nst && !*abort_flag; i++) {
             const int s = i % STAGES, ph = (i / STAGES) & 1;
             if (!mbar_wait(full_raw(s), ph)) {
@@ -307,9 +376,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             const uint8_t* raw = smem + (raw_addr(s) - sbase);
             uint8_t* bt = smem + (b_addr(s) - sbase);
-            for (int q = t; q < CH_IN; q += 128) {
+            uint4 wv[PER];
+#pragma unroll
+            for (int u = 0; u < PER; u++) wv[u] = reinterpret_cast<const uint4*>(raw)[t + 128 * u];
+#pragma unroll
+            for (int u = 0; u < PER; u++) {
+                const int q = t + 128 * u;
                 const int row = q / (RB / 16), c = q % (RB / 16);
-                const uint4 w = *reinterpret_cast<const uint4*>(raw + (size_t)q * 16);
+                const uint4 w = wv[u];
                 const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
                 const int r7 = row & 7;
                 uint8_t* rb = bt + (row >> 3) * 1024 + r7 * 128;
@@ -351,58 +425,79 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         asm volatile("tcgen05.fence::after_thread_sync;");
         const int sub = warp & 3;                 // TMEM lanes 32*sub .. 32*sub+31 = tile rows
         const int m = m0 + sub * 32 + lane;
-        const int m_act = p.m_dev ? min(p.M, *p.m_dev) : p.M;
-        const bool row_ok = m < m_act;
+        const bool in_m = m < p.M;
         const uint32_t tbase = tmem + ((uint32_t)(sub * 32) << 16);
-        if (ok && nst > 0) {
-            for (int j = 0; j < BN / 16; j++) {
-                uint32_t r[P][16];
+        bool write_tile = ok;
+        if (ok && p.splits > 1) {
+            // Split-K: every split adds its partial sums into the workspace,
+            // laid out [plane][n][m] so that a warp's 32 rows are 32 adjacent
+            // words; the split that retires the tile last reads the totals
+            // back, re-zeroes them and runs the epilogue.
+            if (nst > 0) {
+                for (int j = 0; j < BN / 16; j++) {
+                    uint32_t r[P][16];
 #pragma unroll
-                for (int pl = 0; pl < P; pl++) tmem_ld16(tbase + (uint32_t)(pl * BN + j * 16), r[pl]);
-                if (!row_ok) continue;
-                if (p.splits > 1) {
+                    for (int pl = 0; pl < P; pl++) tmem_ld16(tbase + (uint32_t)(pl * BN + j * 16), r[pl]);
+                    if (!in_m) continue;
 #pragma unroll
                     for (int pl = 0; pl < P; pl++)
 #pragma unroll
                         for (int c = 0; c < 16; c++)
                             if (r[pl][c] != 0)
-                                atomicAdd(p.ws + ((size_t)pl * p.M + m) * p.N + n0 + j * 16 + c, (int32_t)r[pl][c]);
-                } else {
-#pragma unroll
-                    for (int c = 0; c < 16; c += 2) {
-                        int32_t a[P], b[P];
-#pragma unroll
-                        for (int pl = 0; pl < P; pl++) {
-                            a[pl] = (int32_t)r[pl][c];
-                            b[pl] = (int32_t)r[pl][c + 1];
-                        }
-                        epi_pair<P, EPI>(p, m, n0 + j * 16 + c, a, b);
-                    }
+                                atomicAdd(p.ws + ((size_t)pl * p.N + n0 + j * 16 + c) * p.M + m, (int32_t)r[pl][c]);
                 }
             }
-        }
-        if (p.splits > 1 && ok) {
-            // The split that retires the tile last applies the epilogue.
             __threadfence();
             asm volatile("bar.sync 1, 128;" ::: "memory");
             const int tile = blockIdx.y * gridDim.x + blockIdx.x;
             if (t == 0) s_last = (atomicAdd(p.counters + tile, 1) == p.splits - 1);
             asm volatile("bar.sync 1, 128;" ::: "memory");
-            if (s_last) {
+            write_tile = s_last != 0;
+            if (write_tile) {
                 __threadfence();
-                if (row_ok) {
-                    for (int nn = 0; nn < BN; nn += 2) {
-                        int32_t a[P], b[P];
-#pragma unroll
-                        for (int pl = 0; pl < P; pl++) {
-                            a[pl] = atomicExch(p.ws + ((size_t)pl * p.M + m) * p.N + n0 + nn, 0);
-                            b[pl] = atomicExch(p.ws + ((size_t)pl * p.M + m) * p.N + n0 + nn + 1, 0);
-                        }
-                        epi_pair<P, EPI>(p, m, n0 + nn, a, b);
-                    }
-                }
                 if (t == 0) p.counters[tile] = 0;
             }
+        }
+        if (write_tile) {
+            // Pass 1: per-column values of this thread's row -> its warp's
+            // staging rows (row stride BN + 4 words: conflict-free).
+            float* stg = reinterpret_cast<float*>(smem) + sub * 32 * Ly::SROW;
+            const float a_s = in_m ? p.a_scale[m] : 0.0f;
+            const float s_all = __fmul_rn(a_s, p.w_scale_all);
+            for (int j = 0; j < BN / 16; j++) {
+                uint32_t r[P][16];
+                if (p.splits > 1) {
+                    // All loads of the chunk are issued before anything is
+                    // written; the workspace is re-zeroed after the tile.
+#pragma unroll
+                    for (int pl = 0; pl < P; pl++)
+#pragma unroll
+                        for (int c = 0; c < 16; c++)
+                            r[pl][c] = in_m ? (uint32_t)__ldcg(p.ws + ((size_t)pl * p.N + n0 + j * 16 + c) * p.M + m)
+                                            : 0u;
+                } else {
+#pragma unroll
+                    for (int pl = 0; pl < P; pl++) tmem_ld16(tbase + (uint32_t)(pl * BN + j * 16), r[pl]);
+                }
+                float v[16];
+#pragma unroll
+                for (int c = 0; c < 16; c++) {
+                    int32_t a[P];
+#pragma unroll
+                    for (int pl = 0; pl < P; pl++) a[pl] = (int32_t)r[pl][c];
+                    v[c] = col_value<P, EPI>(a, a_s, s_wsc[j * 16 + c], s_all);
+                }
+                float4* d = reinterpret_cast<float4*>(stg + lane * Ly::SROW + j * 16);
+#pragma unroll
+                for (int q = 0; q < 4; q++) d[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            }
+            __syncwarp();
+            if (p.splits > 1 && in_m) {
+                for (int pl = 0; pl < P; pl++)
+                    for (int c = 0; c < BN; c++) __stcg(p.ws + ((size_t)pl * p.N + n0 + c) * p.M + m, 0);
+            }
+            // Pass 2: whole rows, 4 adjacent columns per lane, coalesced.
+            store_rows<BN, EPI>(p, stg, m0 + sub * 32, n0, lane);
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;");
@@ -582,6 +677,16 @@ pf_status gemm_tc_launch(const GemmParams& p0, int planes, int plane_rows, cudaS
     PF_CHECK((reinterpret_cast<uintptr_t>(p.A) & 15) == 0 && (reinterpret_cast<uintptr_t>(p.W) & 15) == 0,
              "gemm_tc: operands must be 16-byte aligned");
     PF_CHECK(planes == 1 || planes == 3, "gemm_tc: planes must be 1 or 3");
+    // The epilogue writes 16-byte runs of rows (8-byte runs for the SwiGLU
+    // forms) and reads RoPE angles in pairs.
+    const void* dst = p.epi == EPI_I32 ? (const void*)p.out_i32
+                      : (p.epi == EPI_RESID || p.epi == EPI_MTP_RESID3) ? (const void*)p.resid : (const void*)p.out;
+    PF_CHECK(dst && (reinterpret_cast<uintptr_t>(dst) & 15) == 0 && p.ldo % 4 == 0,
+             "gemm_tc: output must be 16-byte aligned with a row stride that is a multiple of 4");
+    PF_CHECK(p.epi != EPI_QKV || p.rope_cols == 0 ||
+                 (p.head_dim % 4 == 0 && p.rope_cols % 4 == 0 && ((reinterpret_cast<uintptr_t>(p.rope_cos) |
+                                                                    reinterpret_cast<uintptr_t>(p.rope_sin)) & 7) == 0),
+             "gemm_tc: RoPE tables must be 8-byte aligned and head_dim a multiple of 4");
     PF_CHECK(planes == 1 || (plane_rows >= p.M && p.plane_stride == (int64_t)plane_rows * p.lda),
              "gemm_tc: plane layout must be [planes][plane_rows][lda]");
     const bool three = p.epi == EPI_LOGITS3 || p.epi == EPI_MTP_SWIGLU3 || p.epi == EPI_MTP_RESID3;
