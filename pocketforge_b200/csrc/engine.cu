@@ -144,7 +144,10 @@ struct pf_engine {
     // Projections run on the tcgen05 kernel (gemm_tc.cu); digit-plane
     // activations are laid out [3][Mcap][lda].
     pf_status gemm(GemmParams p, int planes) {
-        p.splits = 0;
+        // Whole-K tiles: at these shapes the split-K reduction costs more
+        // than the idle SMs it fills.
+        p.splits = 1;
+        p.pdl = true;
         p.ws = gws;
         p.counters = gcnt;
         p.ws_elems = gws_elems;
@@ -173,7 +176,7 @@ struct pf_engine {
             }
             PF_TRY(kv_quant_rows(qkv, NQKV, NQ, NQ + NK, M, nullptr, G, hd, sl, st));
             if (evicting) PF_TRY(kv_pool_spec(kv, l, rb, sp, st));
-            if (attention_decode_supported(H, G, rb.max_rows))
+            if (attention_decode_supported(kv, H, rb.max_rows))
                 PF_TRY(attention_decode(kv, l, rb, qkv, NQKV, NQ, NQ + NK, H, sl, sp, att, NQ, st));
             else
                 PF_TRY(attention(kv, l, rb, qkv, NQKV, NQ, NQ + NK, H, sl, sp, att, NQ, st));

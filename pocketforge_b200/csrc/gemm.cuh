@@ -44,6 +44,7 @@ struct GemmParams {
     int32_t* ws = nullptr;  // split-K workspace, zero on entry, left zero on exit
     int* counters = nullptr;
     size_t ws_elems = 0, cnt_elems = 0;  // capacities of ws / counters
+    bool pdl = false;        // gemm_tc_launch: programmatic dependent launch
 };
 
 // Scratch needed by a split-K launch (bytes of int32 workspace, counters).

@@ -34,7 +34,8 @@ namespace pf {
 namespace {
 
 constexpr int BM = 128, BK = 128;
-constexpr int NUM_THREADS = 192;  // 6 warps
+constexpr int NUM_UNPACK = 256;                 // warps 2..9: weight unpack, then epilogue
+constexpr int NUM_THREADS = 64 + NUM_UNPACK;  // + warp 0 (TMA) and warp 1 (MMA)
 constexpr uint32_t ERR_TIMEOUT = 16u;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -112,8 +113,8 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-__device__ __forceinline__ uint32_t sext4(uint32_t y) { return y | ((y & 0x08080808u) * 0x1Eu); }
-__device__ __forceinline__ uint32_t sext2(uint32_t y) { return y | ((y & 0x02020202u) * 0x7Eu); }
+// Barrier of the epilogue warps only (named barrier 1).
+__device__ __forceinline__ void named_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NUM_UNPACK) : "memory"); }
 
 // Packed bytes per (row, 128-wide K block) of each format.
 template <int WF>
@@ -133,9 +134,9 @@ struct Layout {
     static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
     static constexpr int WSC_OFF = BAR_OFF + 256;        // BN column scales (fp32)
     static constexpr int SMEM = WSC_OFF + BN * 4 + 1024;  // + alignment slack
-    // Epilogue staging (reuses the stage ring): 4 warps x 32 rows x (BN + 4) fp32.
-    static constexpr int SROW = BN + 4;
-    static_assert(4 * 32 * SROW * 4 <= STAGES * STAGE_BYTES, "staging does not fit the stage ring");
+    // Epilogue staging (reuses the stage ring): 8 warps x 32 rows x (BN/2 + 4) fp32.
+    static constexpr int SROW = BN / 2 + 4;
+    static_assert(8 * 32 * SROW * 4 <= STAGES * STAGE_BYTES, "staging does not fit the stage ring");
     static constexpr int TMEM_COLS = (P * BN <= 32) ? 32 : (P * BN <= 64) ? 64 : (P * BN <= 128) ? 128
                                     : (P * BN <= 256) ? 256 : 512;
 };
@@ -262,6 +263,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     using Ly = Layout<BN, P, WF>;
     constexpr int STAGES = Ly::STAGES;
     constexpr int RB = row_bytes<WF>();
+    constexpr int SHIFT = WF == WF_Q4 ? 4 : (WF == WF_Q2 ? 6 : 0);  // weight position inside its byte
+    constexpr int HALF = BN / 2;                                      // columns per epilogue warp
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t sbase = smem_u32(smem);
@@ -276,6 +279,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     auto b_addr = [&](int s) { return sbase + (uint32_t)(s * Ly::STAGE_BYTES + P * Ly::A_BYTES); };
     auto raw_addr = [&](int s) { return sbase + (uint32_t)(s * Ly::STAGE_BYTES + P * Ly::A_BYTES + Ly::B_BYTES); };
 
+    // The next kernel may start its prologue now; it waits for this grid's
+    // completion before it reads anything this grid writes.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
     const int nkt = p.K / BK;
@@ -286,7 +292,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
             mbar_init(full_raw(s), P + 1);  // one arrival per issuing lane
-            mbar_init(full_b(s), 128);
+            mbar_init(full_b(s), NUM_UNPACK);
             mbar_init(empty(s), 1);
         }
         mbar_init(done, 1);
@@ -319,6 +325,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (lane < STAGES * COPIES) {
             const int s = lane / COPIES, c = lane % COPIES;
             const uint32_t bytes = (uint32_t)(c < P ? Ly::A_BYTES : Ly::RAW_BYTES);
+            // Activations come from the previous kernel: under programmatic
+            // dependent launch, wait for it.  Weights do not, so their
+            // copies may start while it finishes.
+            if (c < P) asm volatile("griddepcontrol.wait;" ::: "memory");
             int last = -1;
             for (int i = s; i < nst && !*abort_flag; i += STAGES) {
                 if (!mbar_wait(empty(s), ((i / STAGES) & 1) ^ 1)) {
@@ -343,7 +353,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             constexpr uint32_t idesc = idesc_i8(BN);
             for (int i = 0; i < nst && !*abort_flag; i++) {
                 const int s = i % STAGES, ph = (i / STAGES) & 1;
-                if (!mbar_wait(full_raw(s), ph) || !mbar_wait(full_b(s), ph)) {
+                // full_b completes only after all 128 unpack threads saw
+                // full_raw (activation and weight copies landed) and
+                // arrived, so it orders the MMAs after both.
+                if (!mbar_wait(full_b(s), ph)) {
                     fail();
                     break;
                 }
@@ -361,13 +374,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             umma_commit(done);  // fires once every issued MMA has completed
         }
     } else {
-        // ---------------- weight unpack (warps 2..5), then epilogue ----------------
-        const int t = threadIdx.x - 64;  // 0..127
+        // ---------------- weight unpack (warps 2..9), then epilogue ----------------
+        const int t = threadIdx.x - 64;  // 0 .. NUM_UNPACK-1
         float* s_wsc = reinterpret_cast<float*>(smem + Ly::WSC_OFF);
-        for (int c = t; c < BN; c += 128) s_wsc[c] = p.w_scale ? p.w_scale[n0 + c] : 1.0f;
+        for (int c = t; c < BN; c += NUM_UNPACK) s_wsc[c] = p.w_scale ? p.w_scale[n0 + c] : 1.0f;
         constexpr int CH_IN = BN * RB / 16;  // 16-byte packed chunks per stage
-        static_assert(CH_IN % 128 == 0, "unpack assumes whole rounds of 128 chunks");
-        constexpr int PER = CH_IN / 128;
+        constexpr int PER = (CH_IN + NUM_UNPACK - 1) / NUM_UNPACK;
+        static_assert(CH_IN % NUM_UNPACK == 0 || PER == 1, "partial rounds only with one chunk per thread");
         for (int i = 0; i < nst && !*abort_flag; i++) {
             const int s = i % STAGES, ph = (i / STAGES) & 1;
             if (!mbar_wait(full_raw(s), ph)) {
@@ -378,31 +391,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint8_t* bt = smem + (b_addr(s) - sbase);
             uint4 wv[PER];
 #pragma unroll
-            for (int u = 0; u < PER; u++) wv[u] = reinterpret_cast<const uint4*>(raw)[t + 128 * u];
+            for (int u = 0; u < PER; u++)
+                if (CH_IN >= NUM_UNPACK || t < CH_IN) wv[u] = reinterpret_cast<const uint4*>(raw)[t + NUM_UNPACK * u];
 #pragma unroll
             for (int u = 0; u < PER; u++) {
-                const int q = t + 128 * u;
+                const int q = t + NUM_UNPACK * u;
+                if (CH_IN < NUM_UNPACK && q >= CH_IN) break;
                 const int row = q / (RB / 16), c = q % (RB / 16);
                 const uint4 w = wv[u];
-                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
                 const int r7 = row & 7;
                 uint8_t* rb = bt + (row >> 3) * 1024 + r7 * 128;
+                // Each weight lands in the top bits of its byte (v * 2^SHIFT, exact
+                // in int8); the epilogue shifts the int32 sums back down.
                 if constexpr (WF == WF_Q4) {
-                    uint4 lo, hi;  // k [32c, 32c+16) and [32c+16, 32c+32)
-                    lo.x = sext4(ws[0] & 0x0F0F0F0Fu); hi.x = sext4((ws[0] >> 4) & 0x0F0F0F0Fu);
-                    lo.y = sext4(ws[1] & 0x0F0F0F0Fu); hi.y = sext4((ws[1] >> 4) & 0x0F0F0F0Fu);
-                    lo.z = sext4(ws[2] & 0x0F0F0F0Fu); hi.z = sext4((ws[2] >> 4) & 0x0F0F0F0Fu);
-                    lo.w = sext4(ws[3] & 0x0F0F0F0Fu); hi.w = sext4((ws[3] >> 4) & 0x0F0F0F0Fu);
+                    constexpr uint32_t HI = 0xF0F0F0F0u;  // k [32c, 32c+16): low nibbles; [32c+16, 32c+32): high
+                    const uint4 lo = make_uint4((w.x << 4) & HI, (w.y << 4) & HI, (w.z << 4) & HI, (w.w << 4) & HI);
+                    const uint4 hi = make_uint4(w.x & HI, w.y & HI, w.z & HI, w.w & HI);
                     *reinterpret_cast<uint4*>(rb + (((2 * c) ^ r7) << 4)) = lo;
                     *reinterpret_cast<uint4*>(rb + (((2 * c + 1) ^ r7) << 4)) = hi;
                 } else if constexpr (WF == WF_Q2) {
+                    constexpr uint32_t HI = 0xC0C0C0C0u;
 #pragma unroll
-                    for (int sft = 0; sft < 4; sft++) {  // k [64c + 16 sft, +16)
-                        uint4 o;
-                        o.x = sext2((ws[0] >> (2 * sft)) & 0x03030303u);
-                        o.y = sext2((ws[1] >> (2 * sft)) & 0x03030303u);
-                        o.z = sext2((ws[2] >> (2 * sft)) & 0x03030303u);
-                        o.w = sext2((ws[3] >> (2 * sft)) & 0x03030303u);
+                    for (int sft = 0; sft < 4; sft++) {  // k [64c + 16 sft, +16): bits [2 sft, 2 sft + 2)
+                        const int sh = 6 - 2 * sft;
+                        const uint4 o = make_uint4((w.x << sh) & HI, (w.y << sh) & HI, (w.z << sh) & HI, (w.w << sh) & HI);
                         *reinterpret_cast<uint4*>(rb + (((4 * c + sft) ^ r7) << 4)) = o;
                     }
                 } else {
@@ -413,17 +425,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mbar_arrive(full_b(s));
         }
         // ---------------- epilogue ----------------
-        // `ok` must be the same for all 128 epilogue threads: the TMEM loads
-        // below are warp-collective and the split-K path uses a named barrier.
+        asm volatile("griddepcontrol.wait;" ::: "memory");  // resid, scales, workspace of earlier kernels
+        // `ok` must be the same for all epilogue threads: the TMEM loads below
+        // are warp-collective and the split-K path uses a named barrier.
         __shared__ int s_ok, s_last;
         const bool okl = !*abort_flag && mbar_wait(done, 0);
         if (!okl) fail();
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        named_sync();
         if (t == 0) s_ok = !*abort_flag;
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        named_sync();
         const bool ok = s_ok != 0;
         asm volatile("tcgen05.fence::after_thread_sync;");
-        const int sub = warp & 3;                 // TMEM lanes 32*sub .. 32*sub+31 = tile rows
+        // Warp w reads TMEM lanes 32*(w%4) .. +31 (tile rows) and one half of
+        // the tile's columns.
+        const int sub = warp & 3;
+        const int c0 = ((warp - 2) >> 2) * HALF;
         const int m = m0 + sub * 32 + lane;
         const bool in_m = m < p.M;
         const uint32_t tbase = tmem + ((uint32_t)(sub * 32) << 16);
@@ -434,24 +450,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             // words; the split that retires the tile last reads the totals
             // back, re-zeroes them and runs the epilogue.
             if (nst > 0) {
-                for (int j = 0; j < BN / 16; j++) {
+                for (int j = 0; j < HALF / 16; j++) {
                     uint32_t r[P][16];
 #pragma unroll
-                    for (int pl = 0; pl < P; pl++) tmem_ld16(tbase + (uint32_t)(pl * BN + j * 16), r[pl]);
+                    for (int pl = 0; pl < P; pl++) tmem_ld16(tbase + (uint32_t)(pl * BN + c0 + j * 16), r[pl]);
                     if (!in_m) continue;
 #pragma unroll
                     for (int pl = 0; pl < P; pl++)
 #pragma unroll
                         for (int c = 0; c < 16; c++)
                             if (r[pl][c] != 0)
-                                atomicAdd(p.ws + ((size_t)pl * p.N + n0 + j * 16 + c) * p.M + m, (int32_t)r[pl][c]);
+                                atomicAdd(p.ws + ((size_t)pl * p.N + n0 + c0 + j * 16 + c) * p.M + m, (int32_t)r[pl][c]);
                 }
             }
             __threadfence();
-            asm volatile("bar.sync 1, 128;" ::: "memory");
+            named_sync();
             const int tile = blockIdx.y * gridDim.x + blockIdx.x;
             if (t == 0) s_last = (atomicAdd(p.counters + tile, 1) == p.splits - 1);
-            asm volatile("bar.sync 1, 128;" ::: "memory");
+            named_sync();
             write_tile = s_last != 0;
             if (write_tile) {
                 __threadfence();
@@ -460,11 +476,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         if (write_tile) {
             // Pass 1: per-column values of this thread's row -> its warp's
-            // staging rows (row stride BN + 4 words: conflict-free).
-            float* stg = reinterpret_cast<float*>(smem) + sub * 32 * Ly::SROW;
+            // staging rows (row stride HALF + 4 words: conflict-free).
+            float* stg = reinterpret_cast<float*>(smem) + (warp - 2) * 32 * Ly::SROW;
             const float a_s = in_m ? p.a_scale[m] : 0.0f;
             const float s_all = __fmul_rn(a_s, p.w_scale_all);
-            for (int j = 0; j < BN / 16; j++) {
+            for (int j = 0; j < HALF / 16; j++) {
                 uint32_t r[P][16];
                 if (p.splits > 1) {
                     // All loads of the chunk are issued before anything is
@@ -473,19 +489,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     for (int pl = 0; pl < P; pl++)
 #pragma unroll
                         for (int c = 0; c < 16; c++)
-                            r[pl][c] = in_m ? (uint32_t)__ldcg(p.ws + ((size_t)pl * p.N + n0 + j * 16 + c) * p.M + m)
+                            r[pl][c] = in_m ? (uint32_t)__ldcg(p.ws + ((size_t)pl * p.N + n0 + c0 + j * 16 + c) * p.M + m)
                                             : 0u;
                 } else {
 #pragma unroll
-                    for (int pl = 0; pl < P; pl++) tmem_ld16(tbase + (uint32_t)(pl * BN + j * 16), r[pl]);
+                    for (int pl = 0; pl < P; pl++) tmem_ld16(tbase + (uint32_t)(pl * BN + c0 + j * 16), r[pl]);
                 }
                 float v[16];
 #pragma unroll
                 for (int c = 0; c < 16; c++) {
                     int32_t a[P];
 #pragma unroll
-                    for (int pl = 0; pl < P; pl++) a[pl] = (int32_t)r[pl][c];
-                    v[c] = col_value<P, EPI>(a, a_s, s_wsc[j * 16 + c], s_all);
+                    for (int pl = 0; pl < P; pl++) a[pl] = (int32_t)r[pl][c] >> SHIFT;  // exact: a multiple of 2^SHIFT
+                    v[c] = col_value<P, EPI>(a, a_s, s_wsc[c0 + j * 16 + c], s_all);
                 }
                 float4* d = reinterpret_cast<float4*>(stg + lane * Ly::SROW + j * 16);
 #pragma unroll
@@ -494,10 +510,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             __syncwarp();
             if (p.splits > 1 && in_m) {
                 for (int pl = 0; pl < P; pl++)
-                    for (int c = 0; c < BN; c++) __stcg(p.ws + ((size_t)pl * p.N + n0 + c) * p.M + m, 0);
+                    for (int c = 0; c < HALF; c++) __stcg(p.ws + ((size_t)pl * p.N + n0 + c0 + c) * p.M + m, 0);
             }
             // Pass 2: whole rows, 4 adjacent columns per lane, coalesced.
-            store_rows<BN, EPI>(p, stg, m0 + sub * 32, n0, lane);
+            store_rows<HALF, EPI>(p, stg, m0 + sub * 32, n0 + c0, lane);
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;");
@@ -561,7 +577,22 @@ pf_status launch_tc(const GemmParams& p, int plane_rows, cudaStream_t st) {
         attr = true;
     }
     dim3 grid(p.N / BN, ceil_div(p.M, BM), p.splits);
-    gemm_tc_kernel<BN, P, WF, EPI><<<grid, NUM_THREADS, Ly::SMEM, st>>>(ta, tb, p, plane_rows, device_error_flag());
+    uint32_t* err = device_error_flag();
+    if (p.pdl) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = grid;
+        cfg.blockDim = dim3(NUM_THREADS);
+        cfg.dynamicSmemBytes = Ly::SMEM;
+        cfg.stream = st;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        PF_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, P, WF, EPI>, ta, tb, p, plane_rows, err));
+    } else {
+        gemm_tc_kernel<BN, P, WF, EPI><<<grid, NUM_THREADS, Ly::SMEM, st>>>(ta, tb, p, plane_rows, err);
+    }
     return launch_check("gemm_tc");
 }
 
@@ -577,10 +608,14 @@ pf_status launch_wf(const GemmParams& p, int plane_rows, cudaStream_t st) {
 template <int BN>
 pf_status launch_bn(const GemmParams& p, int planes, int plane_rows, cudaStream_t st) {
     if (planes == 3) {
-        switch (p.epi) {
-            case EPI_LOGITS3: return launch_wf<BN, 3, EPI_LOGITS3>(p, plane_rows, st);
-            case EPI_MTP_SWIGLU3: return launch_wf<BN, 3, EPI_MTP_SWIGLU3>(p, plane_rows, st);
-            default: return launch_wf<BN, 3, EPI_MTP_RESID3>(p, plane_rows, st);
+        if constexpr (BN <= 128) {  // three planes of 256 columns do not fit TMEM
+            switch (p.epi) {
+                case EPI_LOGITS3: return launch_wf<BN, 3, EPI_LOGITS3>(p, plane_rows, st);
+                case EPI_MTP_SWIGLU3: return launch_wf<BN, 3, EPI_MTP_SWIGLU3>(p, plane_rows, st);
+                default: return launch_wf<BN, 3, EPI_MTP_RESID3>(p, plane_rows, st);
+            }
+        } else {
+            PF_CHECK(false, "gemm_tc: three planes need N tiles of at most 128");
         }
     }
     switch (p.epi) {
@@ -653,10 +688,15 @@ pf_status pack_weights_tc(const int8_t* w, int rows, int cols, int wf, void* pac
     return launch_check("pack_weights_tc");
 }
 
-int gemm_tc_pick_bn(int M, int N) {
-    if (N % 128 != 0) return 64;
-    const int tiles128 = ceil_div(M, BM) * (N / 128);
-    return tiles128 >= 148 ? 128 : 64;
+int gemm_tc_pick_bn(int M, int N, int planes) {
+    // Wider MMAs do more work per issued instruction and per stage barrier
+    // (N = 64 runs below the tensor pipe's rate); narrow only where the wide
+    // tile leaves too few CTAs.  Three accumulator planes of 256 columns do
+    // not fit TMEM.
+    const int mt = ceil_div(M, BM);
+    if (planes == 1 && N % 256 == 0 && mt * (N / 256) >= 100) return 256;
+    if (N % 128 == 0 && mt * (N / 128) >= 40) return 128;
+    return 64;
 }
 
 int gemm_tc_pick_splits(int M, int N, int K, int bn, bool have_ws) {
@@ -691,7 +731,7 @@ pf_status gemm_tc_launch(const GemmParams& p0, int planes, int plane_rows, cudaS
              "gemm_tc: plane layout must be [planes][plane_rows][lda]");
     const bool three = p.epi == EPI_LOGITS3 || p.epi == EPI_MTP_SWIGLU3 || p.epi == EPI_MTP_RESID3;
     PF_CHECK(three == (planes == 3), "gemm_tc: epilogue %d does not take %d planes", p.epi, planes);
-    const int bn = gemm_tc_pick_bn(p.M, p.N);
+    const int bn = gemm_tc_pick_bn(p.M, p.N, planes);
     if (p.splits <= 0) {  // automatic: split K only when the tiles do not fill the GPU and a workspace fits
         p.splits = gemm_tc_pick_splits(p.M, p.N, p.K, bn, p.ws != nullptr && p.counters != nullptr);
         const size_t tiles = (size_t)ceil_div(p.M, BM) * (p.N / bn);
@@ -699,6 +739,7 @@ pf_status gemm_tc_launch(const GemmParams& p0, int planes, int plane_rows, cudaS
     }
     PF_CHECK(p.splits == 1 || (p.ws && p.counters), "gemm_tc: split-K needs a workspace");
     PF_CHECK(p.splits <= p.K / BK, "gemm_tc: more splits than K blocks");
+    if (bn == 256) return launch_bn<256>(p, planes, plane_rows, st);
     if (bn == 128) return launch_bn<128>(p, planes, plane_rows, st);
     return launch_bn<64>(p, planes, plane_rows, st);
 }

@@ -7,7 +7,7 @@ namespace pf {
 // Bytes of a weight matrix in the tensor-core packed layout (gemm_tc.cu).
 size_t packed_bytes_tc(int rows, int cols, int wf);
 pf_status pack_weights_tc(const int8_t* w, int rows, int cols, int wf, void* packed, cudaStream_t st);
-int gemm_tc_pick_bn(int M, int N);
+int gemm_tc_pick_bn(int M, int N, int planes);
 int gemm_tc_pick_splits(int M, int N, int K, int bn, bool have_ws);
 // planes == 3: A holds three digit planes of plane_rows rows each
 // (plane_stride == plane_rows * lda).  p.splits == 0 picks the split count.

@@ -77,8 +77,9 @@ pf_status kv_quant_rows(const float* qkv, int ldqkv, int k_col, int v_col, int M
 pf_status kv_pool_spec(const KvCache& kv, int layer, const RowBatch& rb, SpecPool sp, cudaStream_t stream);
 pf_status attention(const KvCache& kv, int layer, const RowBatch& rb, const float* qkv, int ldqkv, int k_col,
                     int v_col, int H, Staged st, SpecPool sp, float* out, int ldo, cudaStream_t stream);
-// Tensor-core variant for batches of at most 32 / (H/G) rows per sequence.
-bool attention_decode_supported(int H, int G, int max_rows);
+// Tensor-core variant for batches of at most 32 / (H/G) rows per sequence
+// whose sink, in-batch pool entries and earlier rows fit one 32-entry block.
+bool attention_decode_supported(const KvCache& kv, int H, int max_rows);
 pf_status attention_decode(const KvCache& kv, int layer, const RowBatch& rb, const float* qkv, int ldqkv, int k_col,
                            int v_col, int H, Staged st, SpecPool sp, float* out, int ldo, cudaStream_t stream);
 // Commits rows [0, n_commit[b]) of every sequence into the cache, all layers.

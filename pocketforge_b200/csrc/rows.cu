@@ -80,6 +80,7 @@ __global__ void __launch_bounds__(RT) rmsnorm_quant_kernel(const float* __restri
                                                            int n, float eps, int M, const int* m_dev,
                                                            float* __restrict__ normed, int8_t* __restrict__ q,
                                                            float* __restrict__ qs, int ldq) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // lets the next GEMM start its prologue
     __shared__ float sh[33];
     const int row = blockIdx.x, t = threadIdx.x;
     if (!row_active(row, M, m_dev)) return;
@@ -130,6 +131,7 @@ pf_status rmsnorm_quant(const float* x, const float* w, int n, float eps, int M,
 __global__ void __launch_bounds__(RT) quant_rows_kernel(const float* __restrict__ x, int n, int ldx, int M,
                                                         const int* m_dev, int8_t* __restrict__ q, float* __restrict__ qs,
                                                         int ldq) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // lets the next GEMM start its prologue
     __shared__ float sh[33];
     const int row = blockIdx.x, t = threadIdx.x;
     if (!row_active(row, M, m_dev)) return;
@@ -189,6 +191,7 @@ pf_status quant_rows_given(const float* x, int n, int M, const float* s, int8_t*
 __global__ void __launch_bounds__(RT) split_digits_kernel(const float* __restrict__ x, int n, int ldx, int M,
                                                           const int* m_dev, int8_t* __restrict__ q, int64_t plane,
                                                           int ldq, float* __restrict__ qs) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // lets the next GEMM start its prologue
     __shared__ float sh[33];
     const int row = blockIdx.x, t = threadIdx.x;
     if (!row_active(row, M, m_dev)) return;
@@ -262,13 +265,37 @@ __global__ void argmax_kernel(const float* __restrict__ v, int n, int ld, int M,
     const float* r = v + (size_t)row * ld;
     float best = -INFINITY;
     int bi = 0x7fffffff;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float x = r[i];
-        if (x > best) {  // strided scan: earlier index wins ties within a thread
+    auto take = [&](float x, int i) {
+        if (x > best) {  // ascending scan: earlier index wins ties within a thread
             best = x;
             bi = i;
         }
+    };
+    int done = 0;
+    if (((ld | n) & 3) == 0 && (reinterpret_cast<uintptr_t>(v) & 15) == 0) {
+        // 16-byte loads, four in flight per thread before any comparison.
+        const float4* r4 = reinterpret_cast<const float4*>(r);
+        const int n4 = n >> 2;
+        constexpr int U = 4;
+        for (int b = threadIdx.x; b < n4; b += U * blockDim.x) {
+            float4 x[U];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int j = b + u * blockDim.x;
+                x[u] = j < n4 ? r4[j] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+            }
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int i = 4 * (b + u * blockDim.x);
+                take(x[u].x, i);
+                take(x[u].y, i + 1);
+                take(x[u].z, i + 2);
+                take(x[u].w, i + 3);
+            }
+        }
+        done = n;
     }
+    for (int i = done + threadIdx.x; i < n; i += blockDim.x) take(r[i], i);
     for (int o = 16; o >= 1; o >>= 1) {
         const float ob = __shfl_xor_sync(0xffffffffu, best, o);
         const int oi = __shfl_xor_sync(0xffffffffu, bi, o);

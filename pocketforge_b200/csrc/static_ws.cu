@@ -85,7 +85,7 @@ extern "C" pf_status pf_gemm_packed_static(const int8_t* Aq, const float* a_scal
     p.A = Aq; p.lda = K; p.a_scale = a_scale; p.M = M; p.N = N; p.K = K;
     p.W = packed_w; p.wf = wfmt_of_qtype(qtype); p.w_scale = w_scale;
     p.epi = EPI_F32; p.out = C; p.ldo = N;
-    const int bn = gemm_tc_pick_bn(M, N);
+    const int bn = gemm_tc_pick_bn(M, N, 1);
     p.splits = std::min(K / 128, std::max(2, gemm_tc_pick_splits(M, N, K, bn, true)));
     p.ws = a.ws;
     p.counters = a.cnt;
