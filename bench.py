@@ -112,6 +112,33 @@ def algorithmic_bytes_per_step(model, n_seqs, ctx_avg, committed_per_step, K):
     return W + E + H + kv_read + kv_write
 
 
+def profiled_traffic():
+    """DRAM traffic figures measured by ncu, from the committed summaries in
+    profiles/ (lines "bench-traffic: <what> <bytes>")."""
+    out = {}
+    d = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles")
+    if os.path.isdir(d):
+        for f in sorted(os.listdir(d)):
+            if f.endswith((".md", ".txt")):
+                for ln in open(os.path.join(d, f)):
+                    if ln.startswith("bench-traffic:"):
+                        parts = ln.split()
+                        if len(parts) >= 3:
+                            out[parts[1]] = float(parts[2])
+    return out
+
+
+def projection_ops_per_step(model, M, B, K):
+    """int8 MACs x2 of the layer projections (M rows), the tied unembed of
+    the M rows and the MTP chain (B rows, K heads, 3 planes each)."""
+    d, f, nq, nkv = model.n_embd, model.n_ff, model.n_heads * model.head_dim, model.n_kv_heads * model.head_dim
+    per_layer = d * (nq + 2 * nkv) + nq * d + d * 2 * f + f * d
+    layers = 2 * M * per_layer * model.n_layers
+    unembed = 2 * 3 * M * model.n_vocab * d
+    mtp = 2 * 3 * B * K * (3 * d * d + model.n_vocab * d)
+    return layers + unembed + mtp
+
+
 def cpu_baseline(model, seconds_budget=25.0, threads=8):
     """The oracle port (CPU restatement of the Level-B step, one core) on a
     bounded sample: 1 sequence, 4-token prompt, decode steps until ~budget."""
@@ -258,6 +285,14 @@ def main():
     pos1 = eng.read_positions().astype(np.int64)
     tokens = int((pos1 - pos0).sum())
     launches = eng.launches_per_step() * args.steps
+    # ---- per-kernel device time: a second, shorter timed region whose
+    # captured step carries CUDA event pairs around every attention and
+    # projection launch (they serialise the graph, so the step time above is
+    # taken without them).
+    eng.set_kernel_timing(True)
+    eng.run_steps(2)
+    (attn_ms, attn_n), (proj_ms, proj_n) = eng.kernel_times()
+    eng.set_kernel_timing(False)
     if world > 1:
         t = torch.tensor([ms, tokens], dtype=torch.float64, device="cuda")
         mx = t.clone()
@@ -272,6 +307,16 @@ def main():
     bytes_step = algorithmic_bytes_per_step(model, seqs, ctx_avg, committed, K)
     peak, peak_kind = load_peaks()
     achieved = bytes_step / (step_ms * 1e-3) / 1e9
+    # Dominant kernel: attention over the int8 KV cache, one launch per layer,
+    # all sequences; algorithmic bytes = attended entries x 8 kv heads x
+    # (64 K + 64 V + 2 fp32 scales) for one layer.
+    ctx_mid = float(((pos0 + pos1) / 2 + 2 * R).mean())  # the timing steps ran after the timed region
+    attn_bytes = seqs * ctx_mid * model.n_kv_heads * (2 * model.head_dim + 8)
+    attn_us = attn_ms * 1e3 / max(1, attn_n)
+    attn_gbs = attn_bytes / (attn_us * 1e-6) / 1e9
+    proj_bytes = bytes_step - seqs * ctx_avg * kv_entry_bytes(model) - committed * kv_entry_bytes(model)
+    proj_ops = projection_ops_per_step(model, seqs * R, seqs, K)
+    traffic = profiled_traffic()
     clocks = clk.summary()
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
@@ -290,10 +335,23 @@ def main():
                        "l2": "no flush: weights (0.52 GB) + KV read per step exceed the 126 MB L2",
                        "parallelism": f"replicas x{world}"},
             "verify_step_us": step_ms * 1e3,
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
-                         "unit_of_work": "one decode step (CUDA graph launch)",
-                         "algorithmic_bytes_per_step": bytes_step},
+            "roofline": {"bound": "hbm", "achieved": attn_gbs, "peak": peak, "unit": "GB/s",
+                         "frac": attn_gbs / peak, "peak_kind": peak_kind,
+                         "traffic": traffic.get("attn_decode_per_seq_entry", 0.0) * seqs * ctx_mid or None,
+                         "kernel": "attn_decode_kernel: one layer's attention, all sequences x 8 kv heads",
+                         "algorithmic_bytes_per_launch": attn_bytes, "launch_us": attn_us,
+                         "launches_timed": attn_n,
+                         "step": {"achieved": achieved, "frac": achieved / peak,
+                                  "algorithmic_bytes_per_step": bytes_step,
+                                  "traffic": traffic.get("step_per_seq_entry", 0.0) * seqs * ctx_avg
+                                  + traffic.get("step_fixed", 0.0) or None,
+                                  "unit_of_work": "one verify step (CUDA graph launch)"},
+                         "projections": {"ms_per_step": proj_ms, "launches": proj_n,
+                                         "algorithmic_bytes": proj_bytes,
+                                         "achieved_gbs": proj_bytes / (proj_ms * 1e-3) / 1e9,
+                                         "int8_tops": proj_ops / (proj_ms * 1e-3) / 1e12,
+                                         "int8_peak_tops": 4500.0,
+                                         "int8_peak_kind": "nominal dense int8 (2 x the 2.25 PF dense bf16)"}},
             "cpu_baseline": cpu,
             "e2e": e2e,
             "clocks": clocks,

@@ -255,6 +255,15 @@ PF_API pf_status pf_engine_launches_per_step(pf_engine* e, int32_t* kernels);
 /* Device time of the last pf_engine_step / run_steps call, milliseconds. */
 PF_API pf_status pf_engine_last_ms(pf_engine* e, float* ms);
 
+/* Per-kernel timing (no counterpart in the reference): with timing on, the
+ * step graph is recaptured with CUDA event pairs around every attention
+ * launch and every projection GEMM; after a step, pf_engine_kernel_times
+ * returns the summed device milliseconds and launch counts of the last step
+ * for [0] attention and [1] projections.  Timing perturbs the graph (the event
+ * nodes serialise the launches), so measure the step itself with it off. */
+PF_API pf_status pf_engine_set_kernel_timing(pf_engine* e, int32_t on);
+PF_API pf_status pf_engine_kernel_times(pf_engine* e, float* ms, int32_t* launches);
+
 /* ------------------------------------------------------------------ */
 /* Synthetic model (benchmark and test inputs; host memory)             */
 /* ------------------------------------------------------------------ */

@@ -175,6 +175,17 @@ class BatchEngine:
         check(lib().pf_engine_last_ms(self._h, C.byref(v)), "pf_engine_last_ms")
         return float(v.value)
 
+    def set_kernel_timing(self, on: bool) -> None:
+        check(lib().pf_engine_set_kernel_timing(self._h, 1 if on else 0), "pf_engine_set_kernel_timing")
+
+    def kernel_times(self):
+        """Device ms and launch counts of the last step: ((attention_ms, n),
+        (projection_ms, n)); needs set_kernel_timing(True) before the step."""
+        ms = (C.c_float * 2)()
+        n = (C.c_int32 * 2)()
+        check(lib().pf_engine_kernel_times(self._h, ms, n), "pf_engine_kernel_times")
+        return (float(ms[0]), int(n[0])), (float(ms[1]), int(n[1]))
+
     def generate(self, prompts, max_new_tokens: int, seeds=None) -> List[List[int]]:
         """Prefill, then speculative steps until every sequence has max_new_tokens."""
         self.prefill(prompts, seeds)

@@ -48,20 +48,30 @@ __device__ __forceinline__ void mma_s8(int32_t (&c)[4], uint32_t a0, uint32_t a1
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// Integer <-> float conversions and round-to-nearest-even of values below
+// 2^22 in magnitude on the FMA / integer pipes: adding 1.5 * 2^23 leaves the
+// value's nearest integer (ties to even, as rintf) in the low mantissa bits.
+// Every value converted here is below 2^22: digit-plane products sum at most
+// 64 * 127 * 127 terms, and the digits themselves lie in [-127, 127].
+constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+constexpr int kMagicBits = 0x4B400000;
+__device__ __forceinline__ float i2f_small(int32_t a) { return __fsub_rn(__int_as_float(a + kMagicBits), kMagic); }
+
 __device__ __forceinline__ float comb(int32_t a, int32_t b, int32_t c) {
     const float r = 1.0f / 254.0f;
-    return (float)a + ((float)b + (float)c * r) * r;
+    return i2f_small(a) + (i2f_small(b) + i2f_small(c) * r) * r;
 }
 
 __device__ __forceinline__ void digits3(float x, float mul, int& d1, int& d2, int& d3) {
     const float r0 = x * mul;
-    const float f1 = rintf(r0);
-    const float r1 = (r0 - f1) * 254.0f;
-    const float f2 = rintf(r1);
-    const float r2 = (r1 - f2) * 254.0f;
-    d1 = (int)f1;
-    d2 = (int)f2;
-    d3 = (int)fminf(127.0f, fmaxf(-127.0f, rintf(r2)));
+    const float t1 = __fadd_rn(r0, kMagic);  // rint(r0) + magic
+    const float r1 = (r0 - __fsub_rn(t1, kMagic)) * 254.0f;
+    const float t2 = __fadd_rn(r1, kMagic);
+    const float r2 = (r1 - __fsub_rn(t2, kMagic)) * 254.0f;
+    const float t3 = __fadd_rn(r2, kMagic);
+    d1 = __float_as_int(t1) - kMagicBits;
+    d2 = __float_as_int(t2) - kMagicBits;
+    d3 = min(127, max(-127, __float_as_int(t3) - kMagicBits));
 }
 
 __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {

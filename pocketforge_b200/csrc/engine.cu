@@ -122,9 +122,18 @@ struct pf_engine {
     int graph_n = -1;       // sequences the captured step was built for
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     float last_ms = 0.0f;
+    // Optional per-kernel timing: event pairs captured into the step graph
+    // around every attention (category 0) and projection (category 1) launch.
+    static constexpr int kTimedLaunches = 512;
+    bool ktiming = false;
+    std::vector<cudaEvent_t> kev;  // 2 * kTimedLaunches
+    std::vector<int> kev_cat;
+    int kev_used = 0;
+    bool kev_over = false;
 
     ~pf_engine() {
         if (graph) cudaGraphExecDestroy(graph);
+        for (cudaEvent_t v : kev) cudaEventDestroy(v);
         if (ev0) cudaEventDestroy(ev0);
         if (ev1) cudaEventDestroy(ev1);
         for (void* p : owned) cudaFree(p);
@@ -143,6 +152,23 @@ struct pf_engine {
 
     // Projections run on the tcgen05 kernel (gemm_tc.cu); digit-plane
     // activations are laid out [3][Mcap][lda].
+    pf_status tbegin(int cat) {
+        if (!ktiming) return PF_OK;
+        if (kev_used >= kTimedLaunches) {
+            kev_over = true;
+            return PF_OK;
+        }
+        kev_cat[kev_used] = cat;
+        PF_CUDA(cudaEventRecordWithFlags(kev[2 * kev_used], st, cudaEventRecordExternal));
+        return PF_OK;
+    }
+    pf_status tend() {
+        if (!ktiming || kev_used >= kTimedLaunches) return PF_OK;
+        PF_CUDA(cudaEventRecordWithFlags(kev[2 * kev_used + 1], st, cudaEventRecordExternal));
+        kev_used++;
+        return PF_OK;
+    }
+
     pf_status gemm(GemmParams p, int planes) {
         // Whole-K tiles: at these shapes the split-K reduction costs more
         // than the idle SMs it fills.
@@ -152,7 +178,9 @@ struct pf_engine {
         p.counters = gcnt;
         p.ws_elems = gws_elems;
         p.cnt_elems = gcnt_elems;
-        return gemm_tc_launch(p, planes, Mcap, st);
+        PF_TRY(tbegin(1));
+        PF_TRY(gemm_tc_launch(p, planes, Mcap, st));
+        return tend();
     }
 
     // ---- one pass of all layers over a row batch ---------------------------------
@@ -176,10 +204,12 @@ struct pf_engine {
             }
             PF_TRY(kv_quant_rows(qkv, NQKV, NQ, NQ + NK, M, nullptr, G, hd, sl, st));
             if (evicting) PF_TRY(kv_pool_spec(kv, l, rb, sp, st));
+            PF_TRY(tbegin(0));
             if (attention_decode_supported(kv, H, rb.max_rows))
                 PF_TRY(attention_decode(kv, l, rb, qkv, NQKV, NQ, NQ + NK, H, sl, sp, att, NQ, st));
             else
                 PF_TRY(attention(kv, l, rb, qkv, NQKV, NQ, NQ + NK, H, sl, sp, att, NQ, st));
+            PF_TRY(tend());
             PF_TRY(quant_rows(att, NQ, NQ, M, nullptr, xq, xs, NQ, st));
             {
                 GemmParams p;
@@ -260,6 +290,8 @@ struct pf_engine {
 
     // The device work of one decode step (capturable).
     pf_status enqueue_step() {
+        kev_used = 0;
+        kev_over = false;
         const int n = n_seqs, M = n * R;
         StepBufs s = sb;
         s.n_seqs = n;
@@ -1044,6 +1076,36 @@ pf_status pf_engine_launches_per_step(pf_engine* e, int32_t* kernels) {
 pf_status pf_engine_last_ms(pf_engine* e, float* ms) {
     PF_CHECK(e && ms, "pf_engine_last_ms: null argument");
     *ms = e->last_ms;
+    return PF_OK;
+}
+
+pf_status pf_engine_set_kernel_timing(pf_engine* e, int32_t on) {
+    PF_CHECK(e, "pf_engine_set_kernel_timing: null engine");
+    PF_CUDA(cudaSetDevice(e->dev));
+    if (on && e->kev.empty()) {
+        e->kev.resize(2 * pf_engine::kTimedLaunches);
+        e->kev_cat.resize(pf_engine::kTimedLaunches);
+        for (cudaEvent_t& v : e->kev) PF_CUDA(cudaEventCreate(&v));
+    }
+    if ((on != 0) != e->ktiming) e->graph_dirty = true;
+    e->ktiming = on != 0;
+    return PF_OK;
+}
+
+pf_status pf_engine_kernel_times(pf_engine* e, float* ms, int32_t* launches) {
+    PF_CHECK(e && ms && launches, "pf_engine_kernel_times: null argument");
+    PF_CHECK(e->ktiming && !e->graph_dirty, "pf_engine_kernel_times: no step ran with kernel timing on");
+    PF_CHECK(!e->kev_over, "pf_engine_kernel_times: more than %d timed launches in a step", pf_engine::kTimedLaunches);
+    PF_CUDA(cudaSetDevice(e->dev));
+    PF_CUDA(cudaStreamSynchronize(e->st));
+    ms[0] = ms[1] = 0.0f;
+    launches[0] = launches[1] = 0;
+    for (int i = 0; i < e->kev_used; i++) {
+        float t = 0.0f;
+        PF_CUDA(cudaEventElapsedTime(&t, e->kev[2 * i], e->kev[2 * i + 1]));
+        ms[e->kev_cat[i]] += t;
+        launches[e->kev_cat[i]]++;
+    }
     return PF_OK;
 }
 
