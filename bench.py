@@ -92,9 +92,10 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(rows)}
 
 
-def make_prompts(n, length, vocab, seed):
-    rng = np.random.default_rng(seed)
-    return [rng.integers(0, vocab, length).astype(np.int32) for _ in range(n)]
+def make_prompts(ids, length, vocab, seed=1):
+    """Uniform-random prompts, one seeded stream per global sequence id, so
+    any split of the ids over ranks gives the same global workload."""
+    return [np.random.default_rng((seed, int(i))).integers(0, vocab, length).astype(np.int32) for i in ids]
 
 
 def kv_entry_bytes(model):
@@ -218,6 +219,7 @@ def main():
     import torch.distributed as dist
 
     import pocketforge_b200 as pf
+    from pocketforge_b200 import replicas
 
     if world > 1:
         torch.cuda.set_device(local)
@@ -238,8 +240,11 @@ def main():
     sampling = preset.get("sampling")
     if sampling:
         eng.set_sampling(sampling["temperature"], sampling["top_p"], sampling["top_k"], False)
-    prompts = make_prompts(seqs, plen, model.n_vocab, seed=1 + 1000003 * rank)
-    seeds = [sampling["seed"] + rank * seqs + i for i in range(seqs)] if sampling else None
+    # Weak scaling: every rank owns `seqs` sequences of a global batch of
+    # seqs * world; rank r holds the contiguous block of global ids below.
+    g0, g1 = replicas.sequence_slice(seqs * world, world, rank)
+    prompts = make_prompts(range(g0, g1), plen, model.n_vocab)
+    seeds = [sampling["seed"] + i for i in range(g0, g1)] if sampling else None
 
     # ---- end to end through the public API: pinned host prompts -> prefill
     # -> steps with every step's tokens read back to the host.
@@ -258,12 +263,7 @@ def main():
             got += int(n.sum())
         torch.cuda.synchronize()
         el = time.perf_counter() - t0
-        if world > 1:
-            t = torch.tensor([el, got], dtype=torch.float64, device="cuda")
-            mx = t.clone()
-            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-            dist.all_reduce(t, op=dist.ReduceOp.SUM)
-            el, got = float(mx[0]), float(t[1])
+        el, got = replicas.step_totals(el, got)
         e2e = {"value": got / el, "unit": UNIT,
                "h2d_bytes_per_step": int(seqs * plen * 4 / max(1, args.steps)),
                "d2h_bytes_per_step": int(seqs * (R + 1) * 4),
@@ -284,7 +284,7 @@ def main():
     torch.cuda.synchronize()
     pos1 = eng.read_positions().astype(np.int64)
     tokens = int((pos1 - pos0).sum())
-    launches = eng.launches_per_step() * args.steps
+    launches = eng.launches_per_step() * args.steps * world  # every rank launches the same step graph
     # ---- per-kernel device time: a second, shorter timed region whose
     # captured step carries CUDA event pairs around every attention and
     # projection launch (they serialise the graph, so the step time above is
@@ -293,14 +293,8 @@ def main():
     eng.run_steps(2)
     (attn_ms, attn_n), (proj_ms, proj_n) = eng.kernel_times()
     eng.set_kernel_timing(False)
-    if world > 1:
-        t = torch.tensor([ms, tokens], dtype=torch.float64, device="cuda")
-        mx = t.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        ms_max, tokens_all = float(mx[0]), int(t[1])
-    else:
-        ms_max, tokens_all = ms, tokens
+    ms_max, tokens_all = replicas.step_totals(ms, tokens)
+    per_rank = replicas.gather_to_root({"rank": rank, "device_ms": ms, "tokens": tokens})
     step_ms = ms / args.steps
     ctx_avg = float(((pos0 + pos1) / 2).mean())
     committed = (pos1 - pos0).sum() / args.steps
@@ -357,6 +351,8 @@ def main():
             "clocks": clocks,
             "gpu_launches": launches,
         }
+        if world > 1:
+            line["per_rank"] = per_rank
         print(json.dumps(line))
     eng.close()
     if world > 1:

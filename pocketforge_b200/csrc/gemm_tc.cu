@@ -2,21 +2,31 @@
 // int8 activations x packed Q4 / Q2 / int8 weights -> int32 in TMEM
 // (tcgen05.mma.kind::i8), with the epilogues of gemm.cuh.
 //
-// One CTA computes a 128-row x BN-column output tile (optionally one split
-// of K).  Per 128-wide K stage:
-//   warp 0, one thread: TMA loads of the activation tile(s) (128 x 128 B,
-//     128-byte swizzle) and of the packed weight block (BN rows x RB bytes)
-//     into the stage's buffers, completing on full_raw[s];
-//   warps 2..5: unpack the weight block to int8 in shared memory in the
+// One CTA computes a 128-row x BN-column output tile (BN = 64, 128 or 256;
+// optionally one split of K).  Per 128-wide K stage, through a ring of
+// STAGES shared-memory slots:
+//   warp 0: lane s*(P+1)+c issues copy c of every stage that uses slot s —
+//     the activation tile of digit plane c (128 x 128 B, 128-byte swizzle)
+//     or, for c == P, the packed weight block (BN rows x RB bytes) — and
+//     arrives with its byte count on full_raw[s];
+//   warps 2..9: unpack the weight block to int8 in shared memory in the
 //     tensor core's K-major 128-byte-swizzled layout (the layout the TMA
-//     produces for A), fence the generic->async proxy, arrive on full_b[s];
+//     produces for the activations), each weight in the top bits of its byte;
+//     fence the generic->async proxy; arrive on full_b[s];
 //   warp 1, one thread: four tcgen05.mma (K = 32 each) per activation plane
-//     into TMEM, then tcgen05.commit -> empty[s] frees the stage.
-// After the last stage a commit on `done` releases warps 2..5 to read the
+//     into TMEM, then tcgen05.commit -> empty[s] frees the slot.
+// After the last stage a commit on `done` releases warps 2..9 to read the
 // accumulators (tcgen05.ld 32x32b: warp w reads TMEM lanes 32*(w%4)..+31,
-// i.e. output rows) and run the epilogue.  Split-K partial sums go to an
-// int32 workspace with atomics; the CTA that retires a tile last applies the
-// epilogue and re-zeroes the workspace.  No multicast loads are used.
+// i.e. output rows, and one half of the columns), shift the sums back to the
+// weights' scale, and run the epilogue through a shared staging tile so that
+// every global store is a whole-row run.  Split-K partial sums go to an int32
+// workspace laid out [plane][n][m]; the CTA that retires a tile last applies
+// the epilogue and re-zeroes the workspace.  Every TMA load fills only this
+// CTA's own shared memory.
+//
+// Under programmatic dependent launch the weight copies start before the
+// previous kernel has finished; the activation copies and the epilogue wait
+// for it (griddepcontrol.wait).
 //
 // Every mbarrier wait is bounded (about one second of spinning); a timeout
 // latches ERR_TIMEOUT in the device error flag and the CTA drains and frees
