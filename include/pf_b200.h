@@ -148,6 +148,60 @@ PF_API pf_status pf_sample_rows(const float* logits, int32_t M, int32_t n,
                          const pf_sampling_config* cfg, const float* uniforms,
                          int32_t* out, void* stream);
 
+/* ---- single-vector operations behind the forge:: compatibility classes ----
+ * One call at a time, device pointers, the reference's summation order
+ * (one thread walks a row's loop in sequence). */
+
+/* forge::dot_product (src/matmul_neon.cpp:186-207, scalar path): *out = sum a[i]*b[i]. */
+PF_API pf_status pf_dot_f32(const float* a, const float* b, uint32_t n, float* out, void* stream);
+
+/* MTPHeads row products (src/mtp.cpp:66-95, 199-210): y[r] = sum_i x[i] *
+ * ((nibble - 8) * scale[r]), w[rows][cols/2] two values per byte, low first. */
+PF_API pf_status pf_gemv_q4_rows(const float* x, const uint8_t* w, const float* scale, float* y,
+                                 uint32_t rows, uint32_t cols, void* stream);
+
+/* MTPHeads tied unembed (src/mtp.cpp:111-117): y[r] = sum_i x[i] * w[r][i]. */
+PF_API pf_status pf_gemv_f32_rows(const float* x, const float* w, float* y, uint32_t rows,
+                                  uint32_t cols, void* stream);
+
+/* MTPHeads activation (src/mtp.cpp:82-84, 157-159): a = (g / (1 + exp(-g))) * u. */
+PF_API pf_status pf_mtp_silu_mul(const float* g, const float* u, float* a, uint32_t n, void* stream);
+
+/* y += x (the MTP residual, src/mtp.cpp:97-99). */
+PF_API pf_status pf_vec_add(float* y, const float* x, uint32_t n, void* stream);
+
+/* MTPHeads logits without an embedding table (src/mtp.cpp:118-123). */
+PF_API pf_status pf_mtp_placeholder_logits(float* logits, uint32_t vocab, uint32_t head, void* stream);
+
+/* LayerSkipController::hidden_delta (src/layer_skip.cpp:105-113):
+ * *out = sqrt(sum (a-b)^2 / n). */
+PF_API pf_status pf_skip_delta(const float* a, const float* b, uint32_t n, float* out, void* stream);
+
+/* KVCache::store of one (layer, head) entry (src/kv_cache.cpp:59-127): the
+ * caller chooses the destination slot; if ek is not null the slot's previous
+ * entry (ek/eks, ev/evs) is added in double to acc_k / acc_v first, and with
+ * finalize the acc_n accumulated entries' mean becomes pool entry pk/pv and
+ * the accumulators are cleared.  Then k and v are quantized into dk / dv. */
+PF_API pf_status pf_kvu_store(const float* k, const float* v, uint32_t hd, int8_t* dk, float* dks,
+                              int8_t* dv, float* dvs, const int8_t* ek, const float* eks,
+                              const int8_t* ev, const float* evs, double* acc_k, double* acc_v,
+                              uint32_t acc_n, int32_t finalize, int8_t* pk, float* pks, int8_t* pv,
+                              float* pvs, void* stream);
+
+/* KVCache::attention_scores / attention_weighted_sum (src/kv_cache.cpp:129-198)
+ * of one (layer, head): tiers [0] sink, [1] pool, [2] window ring (`ring`
+ * slots, oldest at `head` once counts[2] == ring), counts[t] entries each;
+ * tier pointers are device arrays of [count][hd] int8 and [count] scales.
+ * Scores: out[e] = q . (k_e * ks_e); weighted sum: out[i] = sum_e p[e] * (v_e[i] * vs_e)
+ * over the first min(cnt, total) entries. */
+PF_API pf_status pf_kvu_scores(const int8_t* const* tier_k, const float* const* tier_ks,
+                               const uint32_t* counts, uint32_t ring, uint32_t head, uint32_t hd,
+                               const float* q, float* out, void* stream);
+PF_API pf_status pf_kvu_weighted_sum(const int8_t* const* tier_v, const float* const* tier_vs,
+                                     const uint32_t* counts, uint32_t ring, uint32_t head,
+                                     uint32_t hd, const float* p, uint32_t cnt, float* out,
+                                     void* stream);
+
 /* Packs an int8 weight matrix w[rows][cols] (values of the reference loader,
  * WeightLoader::load_block_with_scales, src/quant_format.cpp:348-425) into the
  * device format of `qtype` (Q4: 4-bit, Q2/Q1.5: 2-bit, Q8: 8-bit).

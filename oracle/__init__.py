@@ -47,8 +47,13 @@ class PfSamplingConfig(C.Structure):
 
 
 def build(quiet: bool = True) -> None:
-    """Builds liboracle.so and, when the reference checkout exists, _ref/libpfref.so."""
-    out = subprocess.run(["make", "-C", HERE, f"REF={REF_CHECKOUT}", "-j8"],
+    """Builds liboracle.so and, when the reference checkout exists,
+    _ref/libpfref.so and (once pocketforge_b200's library is built) the
+    reference's unit tests against the forge:: headers, _ref/forge_tests/."""
+    targets = ["all"]
+    if os.path.exists(os.path.join(os.path.dirname(HERE), "pocketforge_b200", "libforge_b200.so")):
+        targets.append("forge_tests")
+    out = subprocess.run(["make", "-C", HERE, f"REF={REF_CHECKOUT}", "-j8", *targets],
                          capture_output=True, text=True)
     if out.returncode != 0:
         raise RuntimeError("oracle build failed:\n" + out.stdout + out.stderr)

@@ -17,6 +17,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libpf_b200.so")
+FORGE = os.path.join(HERE, "forge")  # the forge:: C++ API over the C ABI
+FORGE_LIB = os.path.join(HERE, "libforge_b200.so")  # the same library under the name forge:: users link
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -31,24 +33,26 @@ def nvcc() -> str:
 
 
 def sources():
-    cu = sorted(f for f in os.listdir(CSRC) if f.endswith(".cu"))
-    cpp = sorted(f for f in os.listdir(CSRC) if f.endswith(".cpp"))
+    cu = sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cu"))
+    cpp = sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cpp"))
+    cpp += sorted(os.path.join(FORGE, f) for f in os.listdir(FORGE) if f.endswith(".cpp"))
     return cu, cpp
 
 
 def _deps_mtime(src: str) -> float:
     m = os.path.getmtime(src)
-    for f in os.listdir(CSRC):
-        if f.endswith((".cuh", ".h", ".hpp")):
-            m = max(m, os.path.getmtime(os.path.join(CSRC, f)))
+    for d in (CSRC, FORGE):
+        for f in os.listdir(d):
+            if f.endswith((".cuh", ".h", ".hpp")):
+                m = max(m, os.path.getmtime(os.path.join(d, f)))
     for root, _, files in os.walk(INCLUDE):
         for f in files:
             m = max(m, os.path.getmtime(os.path.join(root, f)))
     return m
 
 
-def _compile(src: str, force: bool) -> str:
-    path = os.path.join(CSRC, src)
+def _compile(path: str, force: bool) -> str:
+    src = os.path.relpath(path, HERE).replace(os.sep, "_")
     obj = os.path.join(BUILD, src + ".o")
     if not force and os.path.exists(obj) and os.path.getmtime(obj) >= _deps_mtime(path):
         return obj
@@ -72,6 +76,10 @@ def build(force: bool = False, verbose: bool = False) -> str:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed: {' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+    if not os.path.islink(FORGE_LIB):
+        if os.path.exists(FORGE_LIB):
+            os.remove(FORGE_LIB)
+        os.symlink(os.path.basename(LIB), FORGE_LIB)
     if verbose:
         print(LIB)
     return LIB
