@@ -92,6 +92,12 @@ typedef struct pf_sampling_config {
 /* Library                                                              */
 /* ------------------------------------------------------------------ */
 PF_API const char* pf_last_error(void);
+/* The device-side error flags latched by kernels of the current device since
+ * they were last cleared (bits: 1 index out of range, 2 weight value outside
+ * its packed format, 4 token id outside the vocabulary, 8 context full,
+ * 16 pipeline wait timed out); with `clear`, resets them.  Synchronises the
+ * device. */
+PF_API pf_status pf_read_device_error(uint32_t* flags, int32_t clear);
 /* Number of visible devices with compute capability 10.x (0 when none). */
 PF_API int32_t pf_device_count(void);
 /* Bytes of one packed weight matrix on the device for a format. */

@@ -62,6 +62,17 @@ uint32_t* device_error_flag() {
 
 extern "C" const char* pf_last_error(void) { return pf::last_error(); }
 
+extern "C" pf_status pf_read_device_error(uint32_t* flags, int32_t clear) {
+    PF_TRY(pf::require_device());
+    PF_CHECK(flags, "pf_read_device_error: null argument");
+    uint32_t* f = pf::device_error_flag();
+    PF_CHECK(f, "pf_read_device_error: no error flag on this device");
+    PF_CUDA(cudaDeviceSynchronize());
+    PF_CUDA(cudaMemcpy(flags, f, 4, cudaMemcpyDeviceToHost));
+    if (clear) PF_CUDA(cudaMemset(f, 0, 4));
+    return PF_OK;
+}
+
 extern "C" int32_t pf_device_count(void) {
     int n = 0;
     if (cudaGetDeviceCount(&n) != cudaSuccess) {

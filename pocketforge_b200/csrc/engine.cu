@@ -378,6 +378,9 @@ pf_status pf_engine_create(const pf_model_config* c, int32_t max_seqs, int32_t m
     PF_TRY(require_device());
     PF_CUDA(cudaSetDevice(device));
     PF_TRY(require_device());
+    // The device's error latch is shared by every caller on the device;
+    // flags latched before this engine existed are not its errors.
+    if (uint32_t* flag = device_error_flag()) PF_CUDA(cudaMemset(flag, 0, sizeof(uint32_t)));
 
     auto* e = new pf_engine();
     auto fail = [&](pf_status s) {

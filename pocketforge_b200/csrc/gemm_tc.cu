@@ -3,18 +3,20 @@
 // (tcgen05.mma.kind::i8), with the epilogues of gemm.cuh.
 //
 // One CTA computes a 128-row x BN-column output tile (BN = 64, 128 or 256;
-// optionally one split of K).  Per 128-wide K stage, through a ring of
-// STAGES shared-memory slots:
-//   warp 0: lane s*(P+1)+c issues copy c of every stage that uses slot s —
-//     the activation tile of digit plane c (128 x 128 B, 128-byte swizzle)
-//     or, for c == P, the packed weight block (BN rows x RB bytes) — and
-//     arrives with its byte count on full_raw[s];
-//   warps 2..9: unpack the weight block to int8 in shared memory in the
-//     tensor core's K-major 128-byte-swizzled layout (the layout the TMA
-//     produces for the activations), each weight in the top bits of its byte;
-//     fence the generic->async proxy; arrive on full_b[s];
+// optionally one split of K).  Per 128-wide K stage:
+//   warp 0: lane s*(P+1)+c issues copy c of every stage that uses load slot
+//     s — the activation tile of digit plane c (128 x 128 B, 128-byte
+//     swizzle) or, for c == P, the packed weight block (BN rows x RB bytes)
+//     — and arrives with its byte count on full_raw[s];
+//   warps 2..9: unpack the weight block into unpacked-weight buffer b
+//     (= stage % 2) in the tensor core's K-major 128-byte-swizzled layout
+//     (the layout the TMA produces for the activations), each weight in the
+//     top bits of its byte; fence the generic->async proxy; arrive on
+//     b_full[b];
 //   warp 1, one thread: four tcgen05.mma (K = 32 each) per activation plane
-//     into TMEM, then tcgen05.commit -> empty[s] frees the slot.
+//     into TMEM, then tcgen05.commit -> empty[s] and b_empty[b].
+// The load ring has more slots than the two unpacked buffers, so more copies
+// are in flight per shared-memory byte.
 // After the last stage a commit on `done` releases warps 2..9 to read the
 // accumulators (tcgen05.ld 32x32b: warp w reads TMEM lanes 32*(w%4)..+31,
 // i.e. output rows, and one half of the columns), shift the sums back to the
@@ -137,16 +139,22 @@ struct Layout {
     static constexpr int A_BYTES = BM * BK;             // one plane
     static constexpr int RAW_BYTES = BN * row_bytes<WF>();
     static constexpr int B_BYTES = BN * BK;
-    static constexpr int STAGE_BYTES = P * A_BYTES + B_BYTES + ((RAW_BYTES + 1023) / 1024) * 1024;
-    static constexpr int STAGES_MAX = (P == 1) ? 8 : 3;
+    // Load ring: STAGES slots of activation planes + packed weights (what the
+    // TMA has in flight); the unpacked weights get NB buffers of their own,
+    // so the ring can be deeper than the unpack -> MMA hand-off needs.
+    static constexpr int SLOT_BYTES = P * A_BYTES + ((RAW_BYTES + 1023) / 1024) * 1024;
+    static constexpr int NB = 2;
+    static constexpr int STAGES_MAX = (P == 1) ? 8 : 4;
     static constexpr int BUDGET = 220 * 1024;
-    static constexpr int STAGES = (STAGES_MAX * STAGE_BYTES <= BUDGET) ? STAGES_MAX : (BUDGET / STAGE_BYTES);
-    static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+    static constexpr int FIT = (BUDGET - NB * B_BYTES) / SLOT_BYTES;
+    static constexpr int STAGES = STAGES_MAX < FIT ? STAGES_MAX : FIT;
+    static constexpr int B_OFF = STAGES * SLOT_BYTES;
+    static constexpr int BAR_OFF = B_OFF + NB * B_BYTES;
     static constexpr int WSC_OFF = BAR_OFF + 256;        // BN column scales (fp32)
     static constexpr int SMEM = WSC_OFF + BN * 4 + 1024;  // + alignment slack
-    // Epilogue staging (reuses the stage ring): 8 warps x 32 rows x (BN/2 + 4) fp32.
+    // Epilogue staging (reuses the rings): 8 warps x 32 rows x (BN/2 + 4) fp32.
     static constexpr int SROW = BN / 2 + 4;
-    static_assert(8 * 32 * SROW * 4 <= STAGES * STAGE_BYTES, "staging does not fit the stage ring");
+    static_assert(8 * 32 * SROW * 4 <= BAR_OFF, "staging does not fit the rings");
     static constexpr int TMEM_COLS = (P * BN <= 32) ? 32 : (P * BN <= 64) ? 64 : (P * BN <= 128) ? 128
                                     : (P * BN <= 256) ? 256 : 512;
 };
@@ -279,15 +287,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bars = sbase + Ly::BAR_OFF;
-    auto full_raw = [&](int s) { return bars + 8u * s; };
-    auto full_b = [&](int s) { return bars + 8u * (STAGES + s); };
-    auto empty = [&](int s) { return bars + 8u * (2 * STAGES + s); };
-    const uint32_t done = bars + 8u * (3 * STAGES);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Ly::BAR_OFF + 8 * (3 * STAGES + 1));
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Ly::BAR_OFF + 8 * (3 * STAGES + 1) + 8);
-    auto a_addr = [&](int s, int pl) { return sbase + (uint32_t)(s * Ly::STAGE_BYTES + pl * Ly::A_BYTES); };
-    auto b_addr = [&](int s) { return sbase + (uint32_t)(s * Ly::STAGE_BYTES + P * Ly::A_BYTES); };
-    auto raw_addr = [&](int s) { return sbase + (uint32_t)(s * Ly::STAGE_BYTES + P * Ly::A_BYTES + Ly::B_BYTES); };
+    constexpr int NB = Ly::NB;
+    auto full_raw = [&](int s) { return bars + 8u * s; };       // slot s loaded
+    auto empty = [&](int s) { return bars + 8u * (STAGES + s); };  // slot s consumed by the MMAs
+    auto b_full = [&](int b) { return bars + 8u * (2 * STAGES + b); };       // buffer b unpacked
+    auto b_empty = [&](int b) { return bars + 8u * (2 * STAGES + NB + b); };  // buffer b read by the MMAs
+    const uint32_t done = bars + 8u * (2 * STAGES + 2 * NB);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Ly::BAR_OFF + 8 * (2 * STAGES + 2 * NB + 1));
+    volatile int* abort_flag =
+        reinterpret_cast<volatile int*>(smem + Ly::BAR_OFF + 8 * (2 * STAGES + 2 * NB + 1) + 8);
+    auto a_addr = [&](int s, int pl) { return sbase + (uint32_t)(s * Ly::SLOT_BYTES + pl * Ly::A_BYTES); };
+    auto raw_addr = [&](int s) { return sbase + (uint32_t)(s * Ly::SLOT_BYTES + P * Ly::A_BYTES); };
+    auto b_addr = [&](int b) { return sbase + (uint32_t)(Ly::B_OFF + b * Ly::B_BYTES); };
 
     // The next kernel may start its prologue now; it waits for this grid's
     // completion before it reads anything this grid writes.
@@ -302,8 +313,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
             mbar_init(full_raw(s), P + 1);  // one arrival per issuing lane
-            mbar_init(full_b(s), NUM_UNPACK);
             mbar_init(empty(s), 1);
+        }
+        for (int b = 0; b < NB; b++) {
+            mbar_init(b_full(b), NUM_UNPACK);
+            mbar_init(b_empty(b), 1);
         }
         mbar_init(done, 1);
         *abort_flag = 0;
@@ -363,15 +377,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             constexpr uint32_t idesc = idesc_i8(BN);
             for (int i = 0; i < nst && !*abort_flag; i++) {
                 const int s = i % STAGES, ph = (i / STAGES) & 1;
-                // full_b completes only after all 128 unpack threads saw
+                // b_full completes only after every unpack thread saw
                 // full_raw (activation and weight copies landed) and
                 // arrived, so it orders the MMAs after both.
-                if (!mbar_wait(full_b(s), ph)) {
+                const int b = i % NB;
+                if (!mbar_wait(b_full(b), (i / NB) & 1)) {
                     fail();
                     break;
                 }
+                (void)ph;
                 asm volatile("tcgen05.fence::after_thread_sync;");
-                const uint64_t bd = sw128_desc(b_addr(s));
+                const uint64_t bd = sw128_desc(b_addr(b));
 #pragma unroll
                 for (int pl = 0; pl < P; pl++) {
                     const uint64_t ad = sw128_desc(a_addr(s, pl));
@@ -380,6 +396,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         umma_i8(tmem + (uint32_t)(pl * BN), ad + 2 * kk, bd + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
                 }
                 umma_commit(empty(s));
+                umma_commit(b_empty(b));
             }
             umma_commit(done);  // fires once every issued MMA has completed
         }
@@ -393,12 +410,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         static_assert(CH_IN % NUM_UNPACK == 0 || PER == 1, "partial rounds only with one chunk per thread");
         for (int i = 0; i < nst && !*abort_flag; i++) {
             const int s = i % STAGES, ph = (i / STAGES) & 1;
-            if (!mbar_wait(full_raw(s), ph)) {
+            const int b = i % NB;
+            if (!mbar_wait(full_raw(s), ph) || !mbar_wait(b_empty(b), ((i / NB) & 1) ^ 1)) {
                 fail();
                 break;
             }
             const uint8_t* raw = smem + (raw_addr(s) - sbase);
-            uint8_t* bt = smem + (b_addr(s) - sbase);
+            uint8_t* bt = smem + (b_addr(b) - sbase);
             uint4 wv[PER];
 #pragma unroll
             for (int u = 0; u < PER; u++)
@@ -432,7 +450,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_arrive(full_b(s));
+            mbar_arrive(b_full(b));
         }
         // ---------------- epilogue ----------------
         asm volatile("griddepcontrol.wait;" ::: "memory");  // resid, scales, workspace of earlier kernels

@@ -130,10 +130,14 @@ def test_packed_projection_bitexact(qtype, lo, hi, M, N, K):
 def test_pack_rejects_out_of_range():
     W = np.full((8, 128), 9, np.int8)  # 9 does not fit Q4
     packed = torch.zeros(_lib.lib().pf_packed_weight_bytes(8, 128, 1), dtype=torch.uint8, device="cuda")
-    _lib.check(_lib.lib().pf_pack_weights(p(dev(W)), 8, 128, 1, p(packed), None), "pack")
+    L = _lib.lib()
+    flags = C.c_uint32()
+    _lib.check(L.pf_read_device_error(C.byref(flags), 1), "clear")
+    _lib.check(L.pf_pack_weights(p(dev(W)), 8, 128, 1, p(packed), None), "pack")
     torch.cuda.synchronize()
-    # the range error is latched on the device and reported by the engine loaders;
-    # the packed nibbles are the low 4 bits
+    # the range error is latched on the device (the engine loaders report it)
+    _lib.check(L.pf_read_device_error(C.byref(flags), 1), "read")
+    assert flags.value & 2
 
 
 @pytest.mark.parametrize("M,n", [(1, 4), (7, 2048), (320, 2048)])
