@@ -108,6 +108,10 @@ struct pf_engine {
     int32_t* gws = nullptr;
     int* gcnt = nullptr;
     size_t gws_elems = 0, gcnt_elems = 0;
+    // int32 partial products of the K-split residual projections (O, down):
+    // [splits][M][d], summed by resid_rmsnorm_quant.
+    int32_t* rws = nullptr;
+    size_t rws_elems = 0;
 
     pf_sampling_config samp{0.8f, 0.95f, 40, 1};
     std::vector<std::mt19937> rngs;
@@ -184,15 +188,58 @@ struct pf_engine {
     }
 
     // ---- one pass of all layers over a row batch ---------------------------------
+    // A residual projection (O or down) whose K-split int32 slices are still
+    // to be added to x; the next RMSNorm kernel adds them.
+    struct PendingResid {
+        int parts = 0;
+        const float* w_scale = nullptr;
+        const uint8_t* row_skip = nullptr;
+    };
+
+    // O / down projection into rws slices: x += (xq . W^T) * scales happens
+    // in resid_rmsnorm_quant.
+    pf_status resid_gemm(const void* W, int wf, const float* w_scale, int M, int K, const uint8_t* row_skip,
+                         PendingResid* pend) {
+        GemmParams p;
+        p.A = xq; p.lda = K; p.a_scale = xs; p.M = M; p.N = d; p.K = K;
+        p.W = W; p.wf = wf; p.w_scale = w_scale;
+        p.epi = EPI_I32; p.out_i32 = rws; p.ldo = d;
+        p.splits = gemm_tc_slices(M, d, K);
+        p.slice_stride = (int64_t)M * d;
+        PF_CHECK((size_t)p.splits * M * d <= rws_elems, "residual workspace too small");
+        p.pdl = true;
+        PF_TRY(tbegin(1));
+        PF_TRY(gemm_tc_launch(p, 1, Mcap, st));
+        PF_TRY(tend());
+        pend->parts = p.splits;
+        pend->w_scale = w_scale;
+        pend->row_skip = row_skip;
+        return PF_OK;
+    }
+
+    // x += pending residual (if any), then RMSNorm with `norm` + quantization
+    // into xq / xs (norm == nullptr: only the residual).
+    pf_status norm_rows(PendingResid* pend, const float* norm, int M, float* normed) {
+        if (pend->parts == 0) {
+            if (!norm) return PF_OK;
+            return rmsnorm_quant(x, norm, d, cfg.norm_eps, M, nullptr, normed, xq, xs, d, st);
+        }
+        const int parts = pend->parts;
+        pend->parts = 0;
+        return resid_rmsnorm_quant(x, rws, parts, (int64_t)M * d, xs, pend->w_scale, pend->row_skip, norm, d,
+                                   cfg.norm_eps, M, normed, norm ? xq : nullptr, xs, d, st);
+    }
+
     pf_status layers(const RowBatch& rb, int M) {
         const size_t sM = (size_t)Mcap;
+        PendingResid pend;
         for (int l = 0; l < L; l++) {
             Staged sl;
             sl.k = stage.k + (size_t)l * sM * G * 64;
             sl.v = stage.v + (size_t)l * sM * G * 64;
             sl.ks = stage.ks + (size_t)l * sM * G;
             sl.vs = stage.vs + (size_t)l * sM * G;
-            PF_TRY(rmsnorm_quant(x, attn_norm + (size_t)l * d, d, cfg.norm_eps, M, nullptr, nullptr, xq, xs, d, st));
+            PF_TRY(norm_rows(&pend, attn_norm + (size_t)l * d, M, nullptr));
             {
                 GemmParams p;
                 p.A = xq; p.lda = d; p.a_scale = xs; p.M = M; p.N = NQKV; p.K = d;
@@ -211,16 +258,10 @@ struct pf_engine {
                 PF_TRY(attention(kv, l, rb, qkv, NQKV, NQ, NQ + NK, H, sl, sp, att, NQ, st));
             PF_TRY(tend());
             PF_TRY(quant_rows(att, NQ, NQ, M, nullptr, xq, xs, NQ, st));
-            {
-                GemmParams p;
-                p.A = xq; p.lda = NQ; p.a_scale = xs; p.M = M; p.N = d; p.K = NQ;
-                p.W = w_o[l]; p.wf = fmt_o; p.w_scale = s_o[l];
-                p.epi = EPI_RESID; p.resid = x; p.ldo = d;
-                PF_TRY(gemm(p, 1));
-            }
+            PF_TRY(resid_gemm(w_o[l], fmt_o, s_o[l], M, NQ, nullptr, &pend));
             float* normed = skip_on ? normed_all + (size_t)l * sM * d : nullptr;
             uint8_t* skipl = skip_on ? skip_all + (size_t)l * sM : nullptr;
-            PF_TRY(rmsnorm_quant(x, ffn_norm + (size_t)l * d, d, cfg.norm_eps, M, nullptr, normed, xq, xs, d, st));
+            PF_TRY(norm_rows(&pend, ffn_norm + (size_t)l * d, M, normed));
             if (skip_on)
                 PF_TRY(skip_decide(rb.nb, rb.row0, rb.n, normed, d, skip_cache + (size_t)l * d, (size_t)L * d,
                                    layer_threshold(l), skipl, st));
@@ -232,15 +273,9 @@ struct pf_engine {
                 PF_TRY(gemm(p, 1));
             }
             PF_TRY(quant_rows(act, F, F, M, nullptr, xq, xs, F, st));
-            {
-                GemmParams p;
-                p.A = xq; p.lda = F; p.a_scale = xs; p.M = M; p.N = d; p.K = F;
-                p.W = w_down[l]; p.wf = fmt_down; p.w_scale = s_down[l];
-                p.epi = EPI_RESID; p.resid = x; p.ldo = d; p.row_skip = skipl;
-                PF_TRY(gemm(p, 1));
-            }
+            PF_TRY(resid_gemm(w_down[l], fmt_down, s_down[l], M, F, skipl, &pend));
         }
-        return PF_OK;
+        return norm_rows(&pend, nullptr, M, nullptr);  // the last layer's residual
     }
 
     // Tied unembed of n rows of `src` (pre-final-norm hidden) into out [n][V].
@@ -579,6 +614,9 @@ pf_status pf_engine_create(const pf_model_config* c, int32_t max_seqs, int32_t m
     // split-K is only chosen below 2*148 output tiles of 64x64
     e->gws_elems = (size_t)3 * 296 * 64 * 64;
     E_TRY(dalloc(&e->gws, e->gws_elems, o));
+    for (int m = 1; m <= e->Mcap; m++)  // slices of the K-split residual projections, any row count
+        e->rws_elems = std::max(e->rws_elems, (size_t)std::max(gemm_tc_slices(m, d, e->NQ), gemm_tc_slices(m, d, F)) * m * d);
+    E_TRY(dalloc(&e->rws, e->rws_elems, o));
     e->gcnt_elems = 296;
     E_TRY(dalloc(&e->gcnt, e->gcnt_elems, o));
     PF_CUDA(cudaMemset(e->gws, 0, e->gws_elems * 4));

@@ -45,6 +45,10 @@ struct GemmParams {
     int* counters = nullptr;
     size_t ws_elems = 0, cnt_elems = 0;  // capacities of ws / counters
     bool pdl = false;        // gemm_tc_launch: programmatic dependent launch
+    // gemm_tc_launch with EPI_I32: > 0 splits K over `splits` CTAs per tile,
+    // each writing its int32 partial tile to out_i32 + split * slice_stride
+    // (no reduction; the consumer sums the slices).
+    int64_t slice_stride = 0;
 };
 
 // Scratch needed by a split-K launch (bytes of int32 workspace, counters).

@@ -208,7 +208,8 @@ __device__ __forceinline__ void rope_pair(float& x0, float& x1, float c, float s
 // inputs (residual rows, RoPE angles) are fetched for U groups before any of
 // them is written, keeping several loads in flight.
 template <int BN, int EPI>
-__device__ __forceinline__ void store_rows(const GemmParams& p, const float* stg, int rbase, int n0, int lane) {
+__device__ __forceinline__ void store_rows(const GemmParams& p, const float* stg, int rbase, int n0, int lane,
+                                           int32_t* out_i32) {
     constexpr int SROW = BN + 4;
     constexpr int CPR = BN / 4, RPI = 32 / CPR, ITERS = 32 / RPI, U = 4;
     static_assert(ITERS % U == 0, "row groups");
@@ -246,7 +247,7 @@ __device__ __forceinline__ void store_rows(const GemmParams& p, const float* stg
             const int m = rbase + rr[u];
             float4 x = *reinterpret_cast<const float4*>(stg + rr[u] * SROW + 4 * cg);
             if constexpr (EPI == EPI_I32) {
-                *reinterpret_cast<int4*>(p.out_i32 + (size_t)m * p.ldo + n) =
+                *reinterpret_cast<int4*>(out_i32 + (size_t)m * p.ldo + n) =
                     make_int4(__float_as_int(x.x), __float_as_int(x.y), __float_as_int(x.z), __float_as_int(x.w));
             } else if constexpr (EPI == EPI_F32 || EPI == EPI_LOGITS3) {
                 *reinterpret_cast<float4*>(p.out + (size_t)m * p.ldo + n) = x;
@@ -472,7 +473,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const bool in_m = m < p.M;
         const uint32_t tbase = tmem + ((uint32_t)(sub * 32) << 16);
         bool write_tile = ok;
-        if (ok && p.splits > 1) {
+        if (ok && p.splits > 1 && p.slice_stride == 0) {
             // Split-K: every split adds its partial sums into the workspace,
             // laid out [plane][n][m] so that a warp's 32 rows are 32 adjacent
             // words; the split that retires the tile last reads the totals
@@ -510,7 +511,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const float s_all = __fmul_rn(a_s, p.w_scale_all);
             for (int j = 0; j < HALF / 16; j++) {
                 uint32_t r[P][16];
-                if (p.splits > 1) {
+                if (p.splits > 1 && p.slice_stride == 0) {
                     // All loads of the chunk are issued before anything is
                     // written; the workspace is re-zeroed after the tile.
 #pragma unroll
@@ -536,12 +537,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 for (int q = 0; q < 4; q++) d[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
             }
             __syncwarp();
-            if (p.splits > 1 && in_m) {
+            if (p.splits > 1 && p.slice_stride == 0 && in_m) {
                 for (int pl = 0; pl < P; pl++)
                     for (int c = 0; c < HALF; c++) __stcg(p.ws + ((size_t)pl * p.N + n0 + c0 + c) * p.M + m, 0);
             }
             // Pass 2: whole rows, 4 adjacent columns per lane, coalesced.
-            store_rows<HALF, EPI>(p, stg, m0 + sub * 32, n0 + c0, lane);
+            // Slices mode: split z writes its own int32 tile (reduced later).
+            int32_t* oi = p.out_i32 ? p.out_i32 + (size_t)blockIdx.z * p.slice_stride : nullptr;
+            store_rows<HALF, EPI>(p, stg, m0 + sub * 32, n0 + c0, lane, oi);
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;");
@@ -727,6 +730,15 @@ int gemm_tc_pick_bn(int M, int N, int planes) {
     return 64;
 }
 
+int gemm_tc_slices(int M, int N, int K) {
+    // Enough (tile, split) CTAs to cover the SMs once, at most 4 splits of at
+    // least 4 K stages each.
+    const int bn = gemm_tc_pick_bn(M, N, 1);
+    const int tiles = ceil_div(M, BM) * (N / bn);
+    const int s = std::min(148 / std::max(1, tiles), std::min(4, (K / BK) / 4));
+    return std::max(1, s);
+}
+
 int gemm_tc_pick_splits(int M, int N, int K, int bn, bool have_ws) {
     if (!have_ws) return 1;
     const int tiles = ceil_div(M, BM) * (N / bn);
@@ -760,6 +772,14 @@ pf_status gemm_tc_launch(const GemmParams& p0, int planes, int plane_rows, cudaS
     const bool three = p.epi == EPI_LOGITS3 || p.epi == EPI_MTP_SWIGLU3 || p.epi == EPI_MTP_RESID3;
     PF_CHECK(three == (planes == 3), "gemm_tc: epilogue %d does not take %d planes", p.epi, planes);
     const int bn = gemm_tc_pick_bn(p.M, p.N, planes);
+    if (p.slice_stride > 0) {  // split K into separate int32 slices, reduced by the caller's next kernel
+        PF_CHECK(p.epi == EPI_I32 && planes == 1 && p.splits >= 1 && p.splits <= p.K / BK,
+                 "gemm_tc: slices need EPI_I32, one plane and 1..K/128 splits");
+        PF_CHECK(p.slice_stride >= (int64_t)p.M * p.ldo, "gemm_tc: slice stride below M * ldo");
+        if (bn == 256) return launch_bn<256>(p, planes, plane_rows, st);
+        if (bn == 128) return launch_bn<128>(p, planes, plane_rows, st);
+        return launch_bn<64>(p, planes, plane_rows, st);
+    }
     if (p.splits <= 0) {  // automatic: split K only when the tiles do not fill the GPU and a workspace fits
         p.splits = gemm_tc_pick_splits(p.M, p.N, p.K, bn, p.ws != nullptr && p.counters != nullptr);
         const size_t tiles = (size_t)ceil_div(p.M, BM) * (p.N / bn);

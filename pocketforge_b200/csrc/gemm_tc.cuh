@@ -9,6 +9,8 @@ size_t packed_bytes_tc(int rows, int cols, int wf);
 pf_status pack_weights_tc(const int8_t* w, int rows, int cols, int wf, void* packed, cudaStream_t st);
 int gemm_tc_pick_bn(int M, int N, int planes);
 int gemm_tc_pick_splits(int M, int N, int K, int bn, bool have_ws);
+// K splits for a slices-mode launch (GemmParams::slice_stride) of an M x N x K product.
+int gemm_tc_slices(int M, int N, int K);
 // planes == 3: A holds three digit planes of plane_rows rows each
 // (plane_stride == plane_rows * lda).  p.splits == 0 picks the split count.
 pf_status gemm_tc_launch(const GemmParams& p, int planes, int plane_rows, cudaStream_t st);

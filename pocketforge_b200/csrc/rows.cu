@@ -73,34 +73,67 @@ __device__ __forceinline__ bool row_active(int row, int M, const int* m_dev) {
 }  // namespace
 
 // ---------------------------------------------------------------------------
-// RMSNorm (src/matmul_neon.cpp:231-239) fused with the activation quantizer.
-// normed (optional) receives the fp32 output; q/qs the int8 row and scale.
+// RMSNorm (src/matmul_neon.cpp:231-239) fused with the activation quantizer,
+// optionally preceded by the residual add of a K-split projection:
+//   x += ((float)acc * a_scale[row]) * w_scale[col]   (acc = sum of the int32
+//   slices; matmul_quantized's two roundings, src/matmul_neon.cpp:176-180;
+//   rows with row_skip set keep x),
+// then normed (optional) = RMSNorm(x) * w and q/qs its int8 row and scale.
+// Template E = elements per thread (n <= 256 E).  Every load of the row is
+// issued before the first use, without branches, so that a row costs one
+// memory round trip.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(RT) rmsnorm_quant_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                                                           int n, float eps, int M, const int* m_dev,
-                                                           float* __restrict__ normed, int8_t* __restrict__ q,
-                                                           float* __restrict__ qs, int ldq) {
+constexpr int kMaxParts = 4;  // K-split slices summed per element
+
+template <int E>
+__global__ void __launch_bounds__(RT) norm_rows_kernel(
+    float* __restrict__ x, const int32_t* __restrict__ parts, int n_parts, int64_t part_stride,
+    const float* __restrict__ a_s, const float* __restrict__ w_s, const uint8_t* __restrict__ row_skip,
+    const float* __restrict__ w, int n, float eps, int M, const int* m_dev, float* __restrict__ normed,
+    int8_t* __restrict__ q, float* __restrict__ qs, int ldq) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // lets the next GEMM start its prologue
     __shared__ float sh[33];
     const int row = blockIdx.x, t = threadIdx.x;
     if (!row_active(row, M, m_dev)) return;
-    const float* xr = x + (size_t)row * n;
-    float v[EPT];
-    float ss = 0.0f;
+    float* xr = x + (size_t)row * n;
+    const bool add = n_parts > 0 && !(row_skip && row_skip[row]);
+    const int32_t* pr = parts ? parts + (size_t)row * n : nullptr;
+    float v[E], wn[E], ws[E];
+    int32_t acc[E];
 #pragma unroll
-    for (int i = 0; i < EPT; i++) {
+    for (int i = 0; i < E; i++) {
         const int c = t + i * RT;
-        v[i] = c < n ? xr[c] : 0.0f;
-        ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+        const bool in = c < n;
+        v[i] = in ? xr[c] : 0.0f;
+        wn[i] = (in && w) ? w[c] : 0.0f;
+        ws[i] = (in && add) ? w_s[c] : 0.0f;
+        acc[i] = 0;
+#pragma unroll
+        for (int s2 = 0; s2 < kMaxParts; s2++) acc[i] += (in && add && s2 < n_parts) ? __ldcg(pr + s2 * part_stride + c) : 0;
     }
+    float ss = 0.0f;
+    if (add) {
+        const float as = a_s[row];
+#pragma unroll
+        for (int i = 0; i < E; i++) {
+            const int c = t + i * RT;
+            if (c < n) {
+                v[i] = __fadd_rn(v[i], __fmul_rn(__fmul_rn(__int2float_rn(acc[i]), as), ws[i]));
+                xr[c] = v[i];
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < E; i++) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+    if (!w) return;
     ss = block_sum(ss, sh);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
     float amax = 0.0f;
 #pragma unroll
-    for (int i = 0; i < EPT; i++) {
+    for (int i = 0; i < E; i++) {
         const int c = t + i * RT;
         if (c < n) {
-            v[i] = __fmul_rn(__fmul_rn(v[i], inv), w[c]);
+            v[i] = __fmul_rn(__fmul_rn(v[i], inv), wn[i]);
             if (normed) normed[(size_t)row * n + c] = v[i];
             amax = fmaxf(amax, fabsf(v[i]));
         }
@@ -110,18 +143,44 @@ __global__ void __launch_bounds__(RT) rmsnorm_quant_kernel(const float* __restri
     float mul, scale;
     row_quant_params(amax, mul, scale);
 #pragma unroll
-    for (int i = 0; i < EPT; i++) {
+    for (int i = 0; i < E; i++) {
         const int c = t + i * RT;
         if (c < n) q[(size_t)row * ldq + c] = q8(v[i], mul);
     }
     if (t == 0) qs[row] = scale;
 }
 
+static pf_status norm_rows(float* x, const int32_t* parts, int n_parts, int64_t part_stride, const float* a_s,
+                           const float* w_s, const uint8_t* row_skip, const float* w, int n, float eps, int M,
+                           const int* m_dev, float* normed, int8_t* q, float* qs, int ldq, cudaStream_t st) {
+    PF_CHECK(n >= 1 && n <= RT * EPT, "rmsnorm: row length %d outside 1..%d", n, RT * EPT);
+    PF_CHECK(!q || w, "rmsnorm: quantization needs the norm weights");
+    if (n <= RT * 8)
+        norm_rows_kernel<8><<<M, RT, 0, st>>>(x, parts, n_parts, part_stride, a_s, w_s, row_skip, w, n, eps, M, m_dev,
+                                              normed, q, qs, ldq);
+    else if (n <= RT * 16)
+        norm_rows_kernel<16><<<M, RT, 0, st>>>(x, parts, n_parts, part_stride, a_s, w_s, row_skip, w, n, eps, M,
+                                               m_dev, normed, q, qs, ldq);
+    else
+        norm_rows_kernel<EPT><<<M, RT, 0, st>>>(x, parts, n_parts, part_stride, a_s, w_s, row_skip, w, n, eps, M,
+                                                m_dev, normed, q, qs, ldq);
+    return launch_check("rmsnorm");
+}
+
 pf_status rmsnorm_quant(const float* x, const float* w, int n, float eps, int M, const int* m_dev, float* normed,
                         int8_t* q, float* qs, int ldq, cudaStream_t st) {
-    PF_CHECK(n <= RT * EPT, "rmsnorm_quant: row length %d above %d", n, RT * EPT);
-    rmsnorm_quant_kernel<<<M, RT, 0, st>>>(x, w, n, eps, M, m_dev, normed, q, qs, ldq);
-    return launch_check("rmsnorm_quant");
+    PF_CHECK(w, "rmsnorm_quant: norm weights required");
+    // x is only read when no slices are given.
+    return norm_rows(const_cast<float*>(x), nullptr, 0, 0, nullptr, nullptr, nullptr, w, n, eps, M, m_dev, normed, q,
+                     qs, ldq, st);
+}
+
+pf_status resid_rmsnorm_quant(float* x, const int32_t* parts, int n_parts, int64_t part_stride, const float* a_s,
+                              const float* w_s, const uint8_t* row_skip, const float* w, int n, float eps, int M,
+                              float* normed, int8_t* q, float* qs, int ldq, cudaStream_t st) {
+    PF_CHECK(n_parts >= 1 && n_parts <= kMaxParts && part_stride >= (int64_t)M * n, "resid_rmsnorm_quant: bad slices");
+    return norm_rows(x, parts, n_parts, part_stride, a_s, w_s, row_skip, w, n, eps, M, nullptr, normed, q, qs, ldq,
+                     st);
 }
 
 // ---------------------------------------------------------------------------

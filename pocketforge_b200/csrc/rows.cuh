@@ -10,6 +10,11 @@ pf_status dequant_ref(const uint8_t* src, int8_t* dst, int64_t n, int kind, cuda
 
 pf_status rmsnorm_quant(const float* x, const float* w, int n, float eps, int M, const int* m_dev, float* normed,
                         int8_t* q, float* qs, int ldq, cudaStream_t st);
+// x[M][n] += sum of n_parts int32 slices (part_stride apart) * a_s[row] * w_s[col]
+// (rows with row_skip set unchanged), then, if w, RMSNorm + quantization.
+pf_status resid_rmsnorm_quant(float* x, const int32_t* parts, int n_parts, int64_t part_stride, const float* a_s,
+                              const float* w_s, const uint8_t* row_skip, const float* w, int n, float eps, int M,
+                              float* normed, int8_t* q, float* qs, int ldq, cudaStream_t st);
 pf_status quant_rows(const float* x, int n, int ldx, int M, const int* m_dev, int8_t* q, float* qs, int ldq,
                      cudaStream_t st);
 pf_status quant_rows_given(const float* x, int n, int M, const float* s, int8_t* q, float* qs, int ldq,
