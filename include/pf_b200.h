@@ -322,6 +322,11 @@ PF_API pf_status pf_engine_last_ms(pf_engine* e, float* ms);
  * for [0] attention and [1] projections.  Timing perturbs the graph (the event
  * nodes serialise the launches), so measure the step itself with it off. */
 PF_API pf_status pf_engine_set_kernel_timing(pf_engine* e, int32_t on);
+/* Number of CTAs over which the verify attention splits the context of each
+ * (sequence, kv head), 1..8; 0 (the default) picks about two waves of CTAs
+ * for the engine's sequence count.  Results do not depend on it beyond float
+ * rounding. */
+PF_API pf_status pf_engine_set_attention_splits(pf_engine* e, int32_t n);
 PF_API pf_status pf_engine_kernel_times(pf_engine* e, float* ms, int32_t* launches);
 
 /* ------------------------------------------------------------------ */

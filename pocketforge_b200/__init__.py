@@ -175,6 +175,10 @@ class BatchEngine:
         check(lib().pf_engine_last_ms(self._h, C.byref(v)), "pf_engine_last_ms")
         return float(v.value)
 
+    def set_attention_splits(self, n: int) -> None:
+        """CTAs per (sequence, kv head) in the verify attention; 0 = automatic."""
+        check(lib().pf_engine_set_attention_splits(self._h, int(n)), "pf_engine_set_attention_splits")
+
     def set_kernel_timing(self, on: bool) -> None:
         check(lib().pf_engine_set_kernel_timing(self._h, 1 if on else 0), "pf_engine_set_kernel_timing")
 

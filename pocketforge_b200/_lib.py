@@ -96,6 +96,7 @@ def lib():
     sig("pf_engine_last_ms", st, vp, C.POINTER(C.c_float))
     sig("pf_engine_launches_per_step", st, vp, C.POINTER(C.c_int32))
     sig("pf_engine_set_kernel_timing", st, vp, C.c_int32)
+    sig("pf_engine_set_attention_splits", st, vp, C.c_int32)
     sig("pf_read_device_error", st, C.POINTER(C.c_uint32), C.c_int32)
     sig("pf_engine_kernel_times", st, vp, C.POINTER(C.c_float), C.POINTER(C.c_int32))
     sig("pf_synth_matrix", st, u32, i32, i32, i32, i32, i32, vp, vp, vp)

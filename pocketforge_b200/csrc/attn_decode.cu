@@ -3,41 +3,77 @@
 //
 // Same semantics as attention() in attention.cu (KVCache::attention_scores /
 // attention_weighted_sum + Engine::compute_attention, src/kv_cache.cpp:129-198,
-// src/engine.cpp:753-779).  Every int8 entry a row can see goes through int8
+// src/engine.cpp:753-779).  Every int8 entry a row can see goes through
 // tensor-core MMAs, 32 entries (one block) at a time:
 //   scores  S = Q . K^T : Q (fp32 after RoPE) split into three int8 digit
-//           planes per row (x = s(q1 + q2/254 + q3/254^2)); K is the stored
-//           int8; int32 products are exact, recombined in fp32 (~1e-7 rel.).
-//   output  O = P . V   : per block, w = p * v_scale split into three int8
-//           digit planes relative to the row's block maximum; V int8.
-// Blocks are the committed pool blocks, the window-ring blocks, and one
-// extra block assembled in shared memory from the sink entries, the pool
-// entries finalized inside this batch and the batch's own earlier rows
-// (staged), each with the range of query rows that may see it.  The float
-// self term of each row is added when the partial softmax states are merged.
+//           planes per row (x = s(q1 + q2/254 + q3/254^2)), K the stored int8,
+//           mma.sync m16n8k32.s8: the int32 products are exact and are
+//           recombined in fp32 (~1e-7 relative, unbiased);
+//           s_raw = S * k_scale, and the score in log2 units is f * s_raw with
+//           f = s * log2(e) / sqrt(64).
+//   output  O = W . V   : w = p * v_scale / 2^E (E = a power-of-two reference
+//           for the v scales, per warp) split into two fp16 planes, w = hi +
+//           lo (hi truncated to 11 significant bits, lo the fp16-rounded
+//           remainder: ~22 bits), V the stored int8, exact in fp16;
+//           mma.sync m16n8k16 with fp32 accumulators.  Each block's products
+//           start from a zero accumulator (the small plane first) and are added
+//           to the running sums with a rounded fp32 add, so the tensor cores'
+//           accumulation rounding does not build up over the context.
+// Online softmax per row with a lazily raised maximum: the reference point
+// moves only when a block's maximum exceeds it by more than 8 (log2 units),
+// so p = 2^((s_raw - m) f) stays <= 2^8 and the fp16 planes stay in range.
+// Maxima stay in the raw units of the scores, and every exponent is an exact
+// difference of two raw scores times f (as exp(s - max) in the reference):
+// a product f * m, rounded, would cost an ulp of a large number.
 //
-// One CTA per (sequence, kv head), four warps.  The query rows form MT
-// m-tiles of 16; the warps of an m-tile take the blocks of a chunk in turn
-// (4/MT blocks per chunk) and keep their own online-softmax state.  Pool and
-// ring blocks stream through a 4-stage cp.async ring in shared memory.
+// Blocks are the committed pool blocks, the window-ring blocks, and one extra
+// block assembled in shared memory from the sink entries, the pool entries
+// finalized inside this batch and the batch's own earlier rows (staged), each
+// with the range of query rows that may see it.  The float self term of each
+// row is added when the partial softmax states are merged.
 //
-// Fragment layouts (mma.m16n8k32.s8): the k index of an MMA can be any
-// permutation of the reduced dimension as long as A and B agree.
-//   QK: thread (g, t) uses bytes [16t, 16t+16) of K row g and of Q rows g,
-//       g+8; k-step 0 takes bytes 0-7, k-step 1 bytes 8-15.
-//   PV: the QK accumulator of thread (g, t) holds entries 8j + 2t + {0,1}
-//       (j = n8 tile); those 8 values become its A fragment directly, so V is
-//       stored dim-major per 32-entry block with the matching entry order
-//       (kv_vpos in kv.cuh) and every B fragment is one 8-byte load.
+// Grid (sequence, kv head, split).  A split takes a contiguous range of the
+// (sequence, kv head)'s blocks; its four warps take the blocks of the range in
+// turn, each with all query rows (MT m-tiles of 16) and its own cp.async ring,
+// so the block loop has no CTA-wide barrier.  The warps' states are merged in
+// shared memory; with more than one split each split writes its state to a
+// workspace and the last split to arrive (a counter per (sequence, kv head),
+// reset by that split) merges them, adds the self term and writes the output.
+//
+// Fragment layouts: the k index of an MMA can be any permutation of the
+// reduced dimension as long as A and B agree.
+//   QK (m16n8k32): thread (g, t) uses bytes [16t, 16t+16) of K row g and of Q
+//       rows g, g+8; k-step 0 takes bytes 0-7, k-step 1 bytes 8-15.
+//   PV (m16n8k16): the QK accumulator of thread (g, t) holds entries 8j + 2t + {0,1}
+//       (j = n8 tile); tiles 2s, 2s+1 are the A fragment of k-step s, and V is
+//       stored dim-major per 32-entry block in the matching entry order
+//       (kv_vpos in kv.cuh): one 8-byte load per dim row gives both k-steps.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
 #include "kv.cuh"
 
 namespace pf {
 
 namespace {
 
-constexpr int QR = 32;  // padded query rows per CTA
-constexpr int NS = 4;   // cp.async stages
+constexpr int QR = 32;   // padded query rows per CTA
+constexpr int NW = 4;    // warps per CTA
+constexpr int NSW = 3;   // cp.async stages per warp
 constexpr int BIG = 1 << 30;
+constexpr int PART = 68; // floats per (split, row) partial state: m, l, pad, pad, o[64]
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kMaxLead = 8.0f;  // log2 units a block max may exceed the reference before it moves
+
+__device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
 
 __device__ __forceinline__ void mma_s8(int32_t (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                        uint32_t b1) {
@@ -74,9 +110,32 @@ __device__ __forceinline__ void digits3(float x, float mul, int& d1, int& d2, in
     d3 = min(127, max(-127, __float_as_int(t3) - kMagicBits));
 }
 
-__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
-    return (uint32_t)(a & 0xFF) | ((uint32_t)(b & 0xFF) << 8) | ((uint32_t)(c & 0xFF) << 16) | ((uint32_t)(d & 0xFF) << 24);
+// Four int8 (one 32-bit word) -> two fp16x2, exactly: byte u = x ^ 0x80 under
+// the fp16 exponent of 1024 is 1024 + u; subtracting 1152 leaves x.
+__device__ __forceinline__ void i8x4_to_h2(uint32_t x, uint32_t& lo, uint32_t& hi) {
+    x ^= 0x80808080u;
+    const uint32_t a = __byte_perm(x, 0x64646464u, 0x4140);
+    const uint32_t b = __byte_perm(x, 0x64646464u, 0x4342);
+    asm("sub.f16x2 %0, %1, %2;" : "=r"(lo) : "r"(a), "r"(0x64806480u));
+    asm("sub.f16x2 %0, %1, %2;" : "=r"(hi) : "r"(b), "r"(0x64806480u));
 }
+
+__device__ __forceinline__ uint32_t pack_h2(float lo_half, float hi_half) {
+    const __half2 h = __floats2half2_rn(lo_half, hi_half);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+// x = hi + lo: hi keeps 11 significant bits (exact in fp16 for |x| >= 2^-14).
+__device__ __forceinline__ float trunc11(float x) { return __int_as_float(__float_as_int(x) & (int)0xFFFFE000u); }
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+// 2^k for |k| <= 126.
+__device__ __forceinline__ float pow2i(int k) { return __int_as_float((127 + k) << 23); }
+// Exponent e with x in [2^(e-1), 2^e), for finite x > 0.
+__device__ __forceinline__ int exp_of(float x) { return ((__float_as_int(x) >> 23) & 0xFF) - 126; }
 
 __device__ __forceinline__ float quad_max(float v) {
     v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
@@ -116,36 +175,32 @@ struct __align__(16) BlockBuf {
 
 template <int MT>
 struct __align__(16) AttnSmem {
-    static constexpr int WPM = 4 / MT;  // warps (= blocks per chunk) per m-tile
-    int8_t qd[3][QR][64];               // query digit planes
-    float qsc[QR];                      // query scales
-    float s_self[QR];                   // self-term scores (scaled)
-    float v_self[QR][64];               // self-term values
-    BlockBuf ex;                        // the extra block
-    int ex_lo[32], ex_hi[32];           // rows of the sequence that see each extra entry
+    int8_t qd[3][16 * MT][64];  // query digit planes
+    float fr[QR];            // per row: f = s * log2(e) / 8 (0 for padding rows)
+    float s_self[QR];        // self-term score, raw units
+    float v_self[QR][64];    // self-term values
+    BlockBuf ex;             // the extra block
+    int ex_lo[32], ex_hi[32];// rows of the sequence that see each extra entry
     union {
-        BlockBuf stage[NS][WPM];
+        BlockBuf ring[NW][NSW];
         struct {
-            float m[4][QR], l[4][QR];
-            float acc[4][QR][64];
+            float m[NW][QR], l[NW][QR];  // raw-unit maxima, sums
+            float acc[NW][QR][64];       // true-scale weighted sums
         } merge;
     } u;
-};
-
-struct Online {  // running softmax state of one query row held by a lane quad
-    float m, l;
+    float cm[QR], cl[QR];    // the CTA's merged state (with acc in u.merge.acc[0])
+    int last;
 };
 
 }  // namespace
 
 template <int MT>
-__global__ void __launch_bounds__(128, 3) attn_decode_kernel(KvCache kv, int layer, RowBatch rb, const float* __restrict__ qkv,
+__global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int layer, RowBatch rb, const float* __restrict__ qkv,
                                                           int ld, int k_col, int v_col, int H, Staged st, SpecPool sp,
-                                                          float* __restrict__ out, int ldo, uint32_t* err) {
-    constexpr int WPM = 4 / MT;
+                                                          AttnWork aw, float* __restrict__ out, int ldo, uint32_t* err) {
     extern __shared__ __align__(16) uint8_t attn_smem_raw[];
     AttnSmem<MT>& sm = *reinterpret_cast<AttnSmem<MT>*>(attn_smem_raw);
-    const int b = blockIdx.x, g = blockIdx.y;
+    const int b = blockIdx.x, g = blockIdx.y, split = blockIdx.z, nsplit = gridDim.z;
     const int n = rb.n[b];
     if (n == 0) return;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
@@ -160,7 +215,6 @@ __global__ void __launch_bounds__(128, 3) attn_decode_kernel(KvCache kv, int lay
     const int nwin = max(0, L0 - qlo);
     const int s0 = (qlo - kv.S) % kv.Wr;  // ring slot of the oldest window position
     const size_t u = kv.unit(b, layer, g);
-    const float scale = 0.125f;           // 1/sqrt(64)
     const int n_spec = npool - nb0;
     const int n_ex = cs + n_spec + (n - 1);
     if (n_ex > 32 || rows > 16 * MT) {  // excluded by the host; never index past the tiles
@@ -171,49 +225,105 @@ __global__ void __launch_bounds__(128, 3) attn_decode_kernel(KvCache kv, int lay
     const int ring_blocks = (nwin + 31) / 32;
     const int nkv = pool_blocks + ring_blocks;  // blocks that stream from memory
     const int nblk = nkv + (n_ex > 0 ? 1 : 0);
-    const int nchunk = (nblk + WPM - 1) / WPM;
+    const int b_begin = (int)((int64_t)nblk * split / nsplit);
+    const int b_end = (int)((int64_t)nblk * (split + 1) / nsplit);
 
-    // ---- cp.async of chunk c (its pool / ring blocks) into stage c % NS ----
-    auto load_chunk = [&](int c) {
-        BlockBuf* sb = sm.u.stage[c % NS];
+    // ---- this warp's cp.async ring: block of iteration i is b_begin + warp + NW * i ----
+    auto load_block = [&](int i) {
+        const int blk = b_begin + warp + NW * i;
+        if (blk >= b_end || blk >= nkv) return;
+        BlockBuf& bb = sm.u.ring[warp][i % NSW];
+        const bool is_pool = blk < pool_blocks;
+        const int bi = is_pool ? blk : blk - pool_blocks;
+        const size_t e0 = (is_pool ? u * kv.P_pad : u * kv.W_pad) + (size_t)bi * 32;
+        const int8_t* ksrc = (is_pool ? kv.pool_k : kv.ring_k) + e0 * 64;
+        const int8_t* vsrc = (is_pool ? kv.pool_v : kv.ring_v) + e0 * 64;
 #pragma unroll
-        for (int j = 0; j < WPM; j++) {
-            const int blk = c * WPM + j;
-            if (blk >= nkv) break;
-            const bool is_pool = blk < pool_blocks;
-            const int bi = is_pool ? blk : blk - pool_blocks;
-            const size_t e0 = (is_pool ? u * kv.P_pad : u * kv.W_pad) + (size_t)bi * 32;
-            cp16(&sb[j].k[0][0] + tid * 16, (is_pool ? kv.pool_k : kv.ring_k) + e0 * 64 + tid * 16);
-            cp16(sb[j].v + tid * 16, (is_pool ? kv.pool_v : kv.ring_v) + e0 * 64 + tid * 16);
-            if (tid < 8)
-                cp16(sb[j].ks + tid * 4, (is_pool ? kv.pool_ks : kv.ring_ks) + e0 + tid * 4);
-            else if (tid < 16)
-                cp16(sb[j].vs + (tid - 8) * 4, (is_pool ? kv.pool_vs : kv.ring_vs) + e0 + (tid - 8) * 4);
+        for (int c = 0; c < 4; c++) {
+            cp16(&bb.k[0][0] + (lane + 32 * c) * 16, ksrc + (lane + 32 * c) * 16);
+            cp16(bb.v + (lane + 32 * c) * 16, vsrc + (lane + 32 * c) * 16);
         }
+        if (lane < 8)
+            cp16(bb.ks + lane * 4, (is_pool ? kv.pool_ks : kv.ring_ks) + e0 + lane * 4);
+        else if (lane < 16)
+            cp16(bb.vs + (lane - 8) * 4, (is_pool ? kv.pool_vs : kv.ring_vs) + e0 + (lane - 8) * 4);
     };
 #pragma unroll
-    for (int c = 0; c < NS - 1; c++) {
-        if (c < nchunk) load_chunk(c);
+    for (int i = 0; i < NSW - 1; i++) {
+        load_block(i);
         cp_commit();
     }
 
-    // ---- queries -> digit planes; self-term score and value ----
-#pragma unroll 2
-    for (int ri = warp; ri < QR; ri += 4) {
-        float x0 = 0.0f, x1 = 0.0f, k0 = 0.0f, k1 = 0.0f, v0 = 0.0f, v1 = 0.0f;
-        if (ri < rows) {
-            const int hh = ri / n, r = ri % n;
-            const float* row = qkv + (size_t)(row0 + r) * ld;
-            const float* q = row + (size_t)(g + hh * kv.G) * 64;
-            x0 = q[lane];
-            x1 = q[lane + 32];
-            k0 = row[k_col + g * 64 + lane];
-            k1 = row[k_col + g * 64 + lane + 32];
-            v0 = row[v_col + g * 64 + lane];
-            v1 = row[v_col + g * 64 + lane + 32];
+    // ---- the extra block: sink entries, pool entries finalized inside the
+    // batch (visible from the row that finalizes them), staged earlier rows.
+    // Its loads, and the query rows' below, are all issued before first use. ----
+    auto ex_src = [&](int e, const int8_t*& kp, const int8_t*& vp, const float*& ksp, const float*& vsp, int& lo) {
+        if (e < cs) {
+            const size_t o = u * kv.S + e;
+            kp = kv.sink_k + o * 64;
+            vp = kv.sink_v + o * 64;
+            ksp = kv.sink_ks + o;
+            vsp = kv.sink_vs + o;
+            lo = 0;
+        } else if (e < cs + n_spec) {
+            const int j = nb0 + (e - cs);
+            const size_t o = ((size_t)b * kv.G + g) * sp.per + (j - nb0);
+            kp = sp.k + o * 64;
+            vp = sp.v + o * 64;
+            ksp = sp.ks + o;
+            vsp = sp.vs + o;
+            lo = kv.S + kv.Wr + (j + 1) * kv.pb - L0;
+        } else {
+            const int j = e - cs - n_spec;
+            const size_t o = (size_t)(row0 + j) * kv.G + g;
+            kp = st.k + o * 64;
+            vp = st.v + o * 64;
+            ksp = st.ks + o;
+            vsp = st.vs + o;
+            lo = j + 1;
         }
+    };
+    const bool own_ex = nkv >= b_begin && nkv < b_end;  // this split owns the extra block
+    const int ex_e = tid >> 2, ex_q4 = tid & 3;          // entry, dims [16*q4, 16*q4 + 16)
+    uint4 ex_k = make_uint4(0, 0, 0, 0), ex_v = make_uint4(0, 0, 0, 0);
+    float ex_ks = 0.0f, ex_vs = 0.0f;
+    int ex_lo = BIG, ex_hi = -1;
+    if (own_ex && ex_e < n_ex) {
+        const int8_t *kp, *vp;
+        const float *ksp, *vsp;
+        ex_src(ex_e, kp, vp, ksp, vsp, ex_lo);
+        ex_hi = BIG;
+        ex_k = *reinterpret_cast<const uint4*>(kp + 16 * ex_q4);
+        ex_v = *reinterpret_cast<const uint4*>(vp + 16 * ex_q4);
+        ex_ks = *ksp;
+        ex_vs = *vsp;
+    }
+
+    // ---- queries -> fp16 fragment planes; self-term score and value ----
+    constexpr int RPW = 4 * MT;  // query rows per warp: warp + NW * k
+    float qx[RPW][2], kx[RPW][2], vx[RPW][2];
+#pragma unroll
+    for (int k = 0; k < RPW; k++) {
+        const int ri = warp + NW * k;
+        const bool in = ri < rows;
+        const int hh = in ? ri / n : 0, r = in ? ri % n : 0;
+        const float* row = qkv + (size_t)(row0 + r) * ld;
+        const float* q = row + (size_t)(g + hh * kv.G) * 64;
+        qx[k][0] = in ? q[lane] : 0.0f;
+        qx[k][1] = in ? q[lane + 32] : 0.0f;
+        kx[k][0] = in ? row[k_col + g * 64 + lane] : 0.0f;
+        kx[k][1] = in ? row[k_col + g * 64 + lane + 32] : 0.0f;
+        vx[k][0] = in ? row[v_col + g * 64 + lane] : 0.0f;
+        vx[k][1] = in ? row[v_col + g * 64 + lane + 32] : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < RPW; k++) {
+        const int ri = warp + NW * k;
+        const float x0 = qx[k][0], x1 = qx[k][1];
         const float amax = warp_max(fmaxf(fabsf(x0), fabsf(x1)));
-        const float mul = (amax == 0.0f || !isfinite(amax)) ? 0.0f : 127.0f / amax;
+        const bool fin = amax <= 3.0e38f;  // inf / NaN query: every score NaN, as in the reference
+        const float mul = (amax == 0.0f || !fin) ? 0.0f : 127.0f / amax;
+        const float f = !fin ? __int_as_float(0x7fc00000) : (amax / 127.0f) * (0.125f * kLog2e);
         int a1, a2, a3, b1, b2, b3;
         digits3(x0, mul, a1, a2, a3);
         digits3(x1, mul, b1, b2, b3);
@@ -223,254 +333,339 @@ __global__ void __launch_bounds__(128, 3) attn_decode_kernel(KvCache kv, int lay
         sm.qd[0][ri][lane + 32] = (int8_t)b1;
         sm.qd[1][ri][lane + 32] = (int8_t)b2;
         sm.qd[2][ri][lane + 32] = (int8_t)b3;
-        // self term with the float k and v (src/engine.cpp:760-778)
-        const float sc = warp_sum(x0 * k0 + x1 * k1) * scale;
+        // self term with the float k and v (src/engine.cpp:760-778), in raw
+        // units: (q . k) / sqrt(64) / (s / sqrt(64))
+        const float sc = warp_sum(x0 * kx[k][0] + x1 * kx[k][1]) * mul;
         if (lane == 0) {
-            sm.qsc[ri] = !isfinite(amax) ? __int_as_float(0x7fc00000) : amax / 127.0f;
+            sm.fr[ri] = f;
             sm.s_self[ri] = sc;
         }
-        sm.v_self[ri][lane] = v0;
-        sm.v_self[ri][lane + 32] = v1;
+        sm.v_self[ri][lane] = vx[k][0];
+        sm.v_self[ri][lane + 32] = vx[k][1];
     }
 
-    // ---- the extra block: sink entries, pool entries finalized inside the
-    // batch (visible from the row that finalizes them), staged earlier rows ----
-    auto ex_src = [&](int e, const int8_t*& kp, const int8_t*& vp, float& ks, float& vs, int& lo) {
-        if (e < cs) {
-            const size_t o = u * kv.S + e;
-            kp = kv.sink_k + o * 64;
-            vp = kv.sink_v + o * 64;
-            ks = kv.sink_ks[o];
-            vs = kv.sink_vs[o];
-            lo = 0;
-        } else if (e < cs + n_spec) {
-            const int j = nb0 + (e - cs);
-            const size_t o = ((size_t)b * kv.G + g) * sp.per + (j - nb0);
-            kp = sp.k + o * 64;
-            vp = sp.v + o * 64;
-            ks = sp.ks[o];
-            vs = sp.vs[o];
-            lo = kv.S + kv.Wr + (j + 1) * kv.pb - L0;
-        } else {
-            const int j = e - cs - n_spec;
-            const size_t o = (size_t)(row0 + j) * kv.G + g;
-            kp = st.k + o * 64;
-            vp = st.v + o * 64;
-            ks = st.ks[o];
-            vs = st.vs[o];
-            lo = j + 1;
-        }
-    };
-    {
-        const int e = tid >> 2, q4 = tid & 3;  // entry e, dims [16*q4, 16*q4 + 16)
-        uint4 kk = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-        float ks = 0.0f, vs = 0.0f;
-        int lo = BIG, hi = -1;
-        if (e < n_ex) {
-            const int8_t *kp, *vp;
-            ex_src(e, kp, vp, ks, vs, lo);
-            hi = BIG;
-            kk = *reinterpret_cast<const uint4*>(kp + 16 * q4);
-            vv = *reinterpret_cast<const uint4*>(vp + 16 * q4);
-        }
-        *reinterpret_cast<uint4*>(&sm.ex.k[e][16 * q4]) = kk;
-        const uint8_t* vb = reinterpret_cast<const uint8_t*>(&vv);
-        const int pos = kv_vpos(e);
+    if (own_ex) {
+        *reinterpret_cast<uint4*>(&sm.ex.k[ex_e][16 * ex_q4]) = ex_k;
+        const uint8_t* vb = reinterpret_cast<const uint8_t*>(&ex_v);
+        const int pos = kv_vpos(ex_e);
 #pragma unroll
-        for (int i = 0; i < 16; i++) sm.ex.v[(16 * q4 + i) * 32 + pos] = (int8_t)vb[i];
-        if (q4 == 0) {
-            sm.ex.ks[e] = ks;
-            sm.ex.vs[e] = vs;
-            sm.ex_lo[e] = lo;
-            sm.ex_hi[e] = hi;
+        for (int i = 0; i < 16; i++) sm.ex.v[(16 * ex_q4 + i) * 32 + pos] = (int8_t)vb[i];
+        if (ex_q4 == 0) {
+            sm.ex.ks[ex_e] = ex_ks;
+            sm.ex.vs[ex_e] = ex_vs;
+            sm.ex_lo[ex_e] = ex_lo;
+            sm.ex_hi[ex_e] = ex_hi;
         }
     }
     __syncthreads();
 
-    // ---- this warp's m-tile: query fragments and row bookkeeping ----
-    const int mt = warp / WPM, jw = warp % WPM;
-    uint4 qa[3], qb[3];
+    // ---- per-thread rows: (m-tile mt, half h) -> query row mt*16 + gid + 8h ----
+    float fr[MT][2], mref[MT][2], lsum[MT][2];
+    int rr[MT][2];
 #pragma unroll
-    for (int p = 0; p < 3; p++) {
-        qa[p] = *reinterpret_cast<const uint4*>(&sm.qd[p][mt * 16 + gid][16 * tig]);
-        qb[p] = *reinterpret_cast<const uint4*>(&sm.qd[p][mt * 16 + gid + 8][16 * tig]);
-    }
-    int ri2[2], rr2[2];
-    float qs2[2];
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-        ri2[h] = mt * 16 + gid + 8 * h;
-        rr2[h] = ri2[h] < rows ? ri2[h] % n : -1;  // padding row: every entry has lo >= 0
-        qs2[h] = sm.qsc[ri2[h]];
-    }
-    Online st2[2] = {{-INFINITY, 0.0f}, {-INFINITY, 0.0f}};
-    float acc[8][4];
-#pragma unroll
-    for (int nt = 0; nt < 8; nt++)
-#pragma unroll
-        for (int c = 0; c < 4; c++) acc[nt][c] = 0.0f;
-
-    for (int c = 0; c < nchunk; c++) {
-        cp_wait<NS - 2>();
-        __syncthreads();  // chunk c landed; stage (c - 1) % NS is free again
-        if (c + NS - 1 < nchunk) load_chunk(c + NS - 1);
-        cp_commit();
-        const int blk = c * WPM + jw;
-        if (blk >= nblk) continue;
-        const bool is_ex = blk == nkv;
-        const BlockBuf& bb = is_ex ? sm.ex : sm.u.stage[c % NS][jw];
-        // Entries of this thread's accumulator columns: e = 8j + 2*tig + cc,
-        // with the rows [lo, hi] of the sequence that may see them.
-        int lo8[8], hi8[8];
-        float ksv[8], vsv[8];
-#pragma unroll
-        for (int j = 0; j < 4; j++)
-#pragma unroll
-            for (int cc = 0; cc < 2; cc++) {
-                const int e = 8 * j + 2 * tig + cc;
-                int lo = BIG, hi = -1;
-                if (is_ex) {
-                    lo = sm.ex_lo[e];
-                    hi = sm.ex_hi[e];
-                } else if (blk < pool_blocks) {
-                    if (blk * 32 + e < nb0) lo = 0, hi = BIG;
-                } else {
-                    const int slot = (blk - pool_blocks) * 32 + e;
-                    if (slot < kv.Wr) {
-                        const int off = slot >= s0 ? slot - s0 : slot - s0 + kv.Wr;  // (slot - s0) mod Wr
-                        if (off < nwin) lo = 0, hi = qlo + off + kv.Wr - L0;
-                    }
-                }
-                const bool valid = hi >= 0 && lo < BIG;
-                lo8[j * 2 + cc] = lo;
-                hi8[j * 2 + cc] = hi;
-                ksv[j * 2 + cc] = valid ? bb.ks[e] : 0.0f;
-                vsv[j * 2 + cc] = valid ? bb.vs[e] : 0.0f;  // a masked entry must not bring a NaN scale in
-            }
-        // ---- scores ----
-        float s[4][4];  // [n8 tile j][accumulator c]: rows gid (c < 2), gid + 8 (c >= 2)
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const uint4 kf = *reinterpret_cast<const uint4*>(&bb.k[8 * j + gid][16 * tig]);
-            int32_t ac[3][4];
-#pragma unroll
-            for (int p = 0; p < 3; p++) {
-                ac[p][0] = ac[p][1] = ac[p][2] = ac[p][3] = 0;
-                mma_s8(ac[p], qa[p].x, qb[p].x, qa[p].y, qb[p].y, kf.x, kf.y);
-                mma_s8(ac[p], qa[p].z, qb[p].z, qa[p].w, qb[p].w, kf.z, kf.w);
-            }
-#pragma unroll
-            for (int cc = 0; cc < 4; cc++) {
-                const int h = cc >> 1, e2 = j * 2 + (cc & 1);
-                const float v = comb(ac[0][cc], ac[1][cc], ac[2][cc]) * qs2[h] * ksv[e2] * scale;
-                s[j][cc] = (rr2[h] >= lo8[e2] && rr2[h] <= hi8[e2]) ? v : -INFINITY;
-            }
-        }
-        // ---- online softmax update, weights w = p * v_scale ----
-        uint32_t wa[3][4];  // A fragments of the three digit planes
-        float wscale[2];
+    for (int mt = 0; mt < MT; mt++)
 #pragma unroll
         for (int h = 0; h < 2; h++) {
-            float bm = -INFINITY;
+            const int ri = mt * 16 + gid + 8 * h;
+            fr[mt][h] = sm.fr[ri];
+            rr[mt][h] = ri < rows ? ri % n : -1;  // padding row: every entry has lo >= 0
+            mref[mt][h] = -INFINITY;
+            lsum[mt][h] = 0.0f;
+        }
+    float acc[MT][8][4];
 #pragma unroll
-            for (int j = 0; j < 4; j++)
+    for (int mt = 0; mt < MT; mt++)
 #pragma unroll
-                for (int cc = 0; cc < 2; cc++) bm = fmaxf(bm, s[j][h * 2 + cc]);
-            bm = quad_max(bm);
-            const float m_new = fmaxf(st2[h].m, bm);
-            float corr = 1.0f;
-            float pw[8];
-            float psum = 0.0f, wmax = 0.0f;
-            if (m_new == -INFINITY) {
+        for (int nt = 0; nt < 8; nt++)
 #pragma unroll
-                for (int k = 0; k < 8; k++) pw[k] = 0.0f;
-            } else {
-                corr = (st2[h].m == -INFINITY) ? 0.0f : __expf(st2[h].m - m_new);
-#pragma unroll
-                for (int j = 0; j < 4; j++)
-#pragma unroll
-                    for (int cc = 0; cc < 2; cc++) {
-                        const float sv = s[j][h * 2 + cc];
-                        const float p = (sv == -INFINITY) ? 0.0f : __expf(sv - m_new);
-                        psum += p;
-                        pw[j * 2 + cc] = p * vsv[j * 2 + cc];
-                        wmax = fmaxf(wmax, fabsf(pw[j * 2 + cc]));
-                    }
-            }
-            psum = quad_sum(psum);
-            wmax = quad_max(wmax);
-            st2[h].l = st2[h].l * corr + psum;
-            st2[h].m = m_new;
-#pragma unroll
-            for (int nt = 0; nt < 8; nt++) {
-                acc[nt][h * 2] *= corr;
-                acc[nt][h * 2 + 1] *= corr;
-            }
-            const float mul = (wmax == 0.0f || !isfinite(wmax)) ? 0.0f : 127.0f / wmax;
-            wscale[h] = wmax / 127.0f;
-            int d[3][8];
-#pragma unroll
-            for (int k = 0; k < 8; k++) digits3(pw[k], mul, d[0][k], d[1][k], d[2][k]);
-            // a0/a1 (k = 4*tig + 0..3): tiles 0,1; a2/a3 (k = 16 + 4*tig + 0..3): tiles 2,3
-#pragma unroll
-            for (int p = 0; p < 3; p++) {
-                wa[p][h] = pack4(d[p][0], d[p][1], d[p][2], d[p][3]);
-                wa[p][2 + h] = pack4(d[p][4], d[p][5], d[p][6], d[p][7]);
+            for (int c = 0; c < 4; c++) acc[mt][nt][c] = 0.0f;
+    int eref = 0;
+    bool have_ref = false;
+
+    for (int i = 0;; i++) {
+        const int blk = b_begin + warp + NW * i;
+        if (blk >= b_end) break;
+        cp_wait<NSW - 2>();
+        __syncwarp();  // every lane's copies of block i landed; stage (i - 1) % NSW is free
+        load_block(i + NSW - 1);
+        cp_commit();
+        const bool is_ex = blk == nkv;
+        const BlockBuf& bb = is_ex ? sm.ex : sm.u.ring[warp][i % NSW];
+
+        // ---- visibility of entry `lane`: query rows [lo, hi] of the sequence ----
+        int lo = BIG, hi = -1;
+        if (is_ex) {
+            lo = sm.ex_lo[lane];
+            hi = sm.ex_hi[lane];
+        } else if (blk < pool_blocks) {
+            if (blk * 32 + lane < nb0) lo = 0, hi = BIG;
+        } else {
+            const int slot = (blk - pool_blocks) * 32 + lane;
+            if (slot < kv.Wr) {
+                const int off = slot >= s0 ? slot - s0 : slot - s0 + kv.Wr;  // (slot - s0) mod Wr
+                if (off < nwin) lo = 0, hi = qlo + off + kv.Wr - L0;
             }
         }
+        const bool valid = hi >= 0 && lo < BIG;
+        const bool full = __all_sync(0xffffffffu, valid && lo <= 0 && hi >= n - 1);
+
+        // ---- v-scale reference: a power of two per warp, raised when a block's
+        // scales outgrow it (the accumulators are rescaled exactly) ----
+        const float vmax = warp_max(valid ? bb.vs[lane] : 0.0f);
+        if (vmax > 0.0f && vmax <= 3.0e38f) {
+            const int ev = exp_of(vmax);
+            if (!have_ref) {
+                eref = ev;
+                have_ref = true;
+            } else if (ev > eref + 4) {
+                const float c = pow2i(max(eref - ev, -126));
+#pragma unroll
+                for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+                    for (int nt = 0; nt < 8; nt++)
+#pragma unroll
+                        for (int c4 = 0; c4 < 4; c4++) acc[mt][nt][c4] *= c;
+                eref = ev;
+            }
+        }
+        const float vmul = pow2i(-max(-126, min(126, eref)));
+
+        // ---- this thread's entries e = 8j + 2*tig + cc: scales (and masks) ----
+        float ksv[8], vsn[8];
+        int lo8[8], hi8[8];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const float2 k2 = *reinterpret_cast<const float2*>(&bb.ks[8 * j + 2 * tig]);
+            const float2 v2 = *reinterpret_cast<const float2*>(&bb.vs[8 * j + 2 * tig]);
+            ksv[2 * j] = k2.x;
+            ksv[2 * j + 1] = k2.y;
+            vsn[2 * j] = v2.x * vmul;
+            vsn[2 * j + 1] = v2.y * vmul;
+        }
+        if (!full) {
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const int e = 8 * (k >> 1) + 2 * tig + (k & 1);
+                lo8[k] = __shfl_sync(0xffffffffu, lo, e);
+                hi8[k] = __shfl_sync(0xffffffffu, hi, e);
+                if (!(hi8[k] >= 0 && lo8[k] < BIG)) vsn[k] = 0.0f;  // a masked entry must not bring a NaN scale in
+            }
+        }
+
+        // ---- scores: S = Q . K^T (three digit planes, exact int32), s_raw = S * k_scale ----
+        float s[MT][4][4];
+#pragma unroll
+        for (int mt = 0; mt < MT; mt++) {
+            uint4 qa[3], qb[3];
+#pragma unroll
+            for (int p = 0; p < 3; p++) {
+                qa[p] = *reinterpret_cast<const uint4*>(&sm.qd[p][mt * 16 + gid][16 * tig]);
+                qb[p] = *reinterpret_cast<const uint4*>(&sm.qd[p][mt * 16 + gid + 8][16 * tig]);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const uint4 kf = *reinterpret_cast<const uint4*>(&bb.k[8 * j + gid][16 * tig]);
+                int32_t ac[3][4];
+#pragma unroll
+                for (int p = 0; p < 3; p++) {
+                    ac[p][0] = ac[p][1] = ac[p][2] = ac[p][3] = 0;
+                    mma_s8(ac[p], qa[p].x, qb[p].x, qa[p].y, qb[p].y, kf.x, kf.y);
+                    mma_s8(ac[p], qa[p].z, qb[p].z, qa[p].w, qb[p].w, kf.z, kf.w);
+                }
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    const int k = 2 * j + (c & 1);
+                    float v = comb(ac[0][c], ac[1][c], ac[2][c]) * ksv[k];
+                    if (!full) {
+                        const int r = rr[mt][c >> 1];
+                        if (!(r >= lo8[k] && r <= hi8[k])) v = -INFINITY;
+                    }
+                    s[mt][j][c] = v;
+                }
+            }
+        }
+
+        // ---- online softmax with a lazily raised reference maximum ----
+        float bmax[MT][2];
+        bool need = false;
+#pragma unroll
+        for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                float bm = -INFINITY;
+#pragma unroll
+                for (int j = 0; j < 4; j++) bm = fmaxf(bm, fmaxf(s[mt][j][2 * h], s[mt][j][2 * h + 1]));
+                bm = quad_max(bm);
+                bmax[mt][h] = bm;
+                const float m = mref[mt][h];
+                need |= (bm > -INFINITY) && (m == -INFINITY || (bm - m) * fr[mt][h] > kMaxLead);
+            }
+        if (__any_sync(0xffffffffu, need)) {
+#pragma unroll
+            for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const float m = mref[mt][h];
+                    const float mn = fmaxf(m, bmax[mt][h]);
+                    if (mn > m) {
+                        const float corr = (m == -INFINITY) ? 0.0f : ex2((m - mn) * fr[mt][h]);
+                        lsum[mt][h] *= corr;
+#pragma unroll
+                        for (int nt = 0; nt < 8; nt++) {
+                            acc[mt][nt][2 * h] *= corr;
+                            acc[mt][nt][2 * h + 1] *= corr;
+                        }
+                        mref[mt][h] = mn;
+                    }
+                }
+        }
+        // p = 2^((s_raw - m) f), w = p * v_scale / 2^E -> two fp16 planes (A fragments)
+        uint32_t wa[MT][2][2][4];  // [m-tile][k-step][plane][reg]
+#pragma unroll
+        for (int mt = 0; mt < MT; mt++) {
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                float w[4];
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    const int h = c >> 1;
+                    const float sv = s[mt][j][c];
+                    const float p = (sv == -INFINITY) ? 0.0f : ex2((sv - mref[mt][h]) * fr[mt][h]);
+                    lsum[mt][h] += p;
+                    w[c] = p * vsn[2 * j + (c & 1)];
+                }
+                const float h0 = trunc11(w[0]), h1 = trunc11(w[1]), h2 = trunc11(w[2]), h3 = trunc11(w[3]);
+                const int ks = j >> 1, r0 = (j & 1) * 2;  // tiles 2s / 2s+1 -> a0,a1 / a2,a3
+                wa[mt][ks][0][r0] = pack_h2(h0, h1);
+                wa[mt][ks][0][r0 + 1] = pack_h2(h2, h3);
+                wa[mt][ks][1][r0] = pack_h2(w[0] - h0, w[1] - h1);
+                wa[mt][ks][1][r0 + 1] = pack_h2(w[2] - h2, w[3] - h3);
+            }
+        }
+
         // ---- O += W . V ----
 #pragma unroll
         for (int nt = 0; nt < 8; nt++) {
             const uint2 vf = *reinterpret_cast<const uint2*>(&bb.v[(nt * 8 + gid) * 32 + 8 * tig]);
-            int32_t o[3][4];
+            uint32_t vb[2][2];
+            i8x4_to_h2(vf.x, vb[0][0], vb[0][1]);
+            i8x4_to_h2(vf.y, vb[1][0], vb[1][1]);
 #pragma unroll
-            for (int p = 0; p < 3; p++) {
-                o[p][0] = o[p][1] = o[p][2] = o[p][3] = 0;
-                // A regs: a0 row g (k low), a1 row g+8 (k low), a2 row g (k high), a3 row g+8 (k high)
-                mma_s8(o[p], wa[p][0], wa[p][1], wa[p][2], wa[p][3], vf.x, vf.y);
+            for (int mt = 0; mt < MT; mt++) {
+                float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                for (int p = 1; p >= 0; p--)  // the remainder plane first
+#pragma unroll
+                    for (int ks = 0; ks < 2; ks++)
+                        mma_f16(o, wa[mt][ks][p][0], wa[mt][ks][p][1], wa[mt][ks][p][2], wa[mt][ks][p][3], vb[ks][0],
+                                vb[ks][1]);
+#pragma unroll
+                for (int c = 0; c < 4; c++) acc[mt][nt][c] += o[c];
             }
-#pragma unroll
-            for (int cc = 0; cc < 4; cc++) acc[nt][cc] += comb(o[0][cc], o[1][cc], o[2][cc]) * wscale[cc >> 1];
         }
     }
     cp_wait<0>();
-    __syncthreads();  // the stage ring becomes the merge area
+    __syncthreads();  // every warp left its ring: the ring area becomes the merge area
 
-    // ---- partial states of the warps -> shared memory ----
+    // ---- warp states -> shared memory (raw-unit maxima, true-scale sums) ----
+    {
+        const float vs_scale = pow2i(max(-126, min(126, eref)));
 #pragma unroll
-    for (int h = 0; h < 2; h++) {
-        const int r = ri2[h];
-        if (tig == 0) {
-            sm.u.merge.m[warp][r] = st2[h].m;
-            sm.u.merge.l[warp][r] = st2[h].l;
-        }
+        for (int mt = 0; mt < MT; mt++)
 #pragma unroll
-        for (int nt = 0; nt < 8; nt++) {
-            sm.u.merge.acc[warp][r][nt * 8 + 2 * tig] = acc[nt][h * 2];
-            sm.u.merge.acc[warp][r][nt * 8 + 2 * tig + 1] = acc[nt][h * 2 + 1];
-        }
+            for (int h = 0; h < 2; h++) {
+                const int r = mt * 16 + gid + 8 * h;
+                const float l = quad_sum(lsum[mt][h]);
+                if (tig == 0) {
+                    sm.u.merge.m[warp][r] = mref[mt][h];
+                    sm.u.merge.l[warp][r] = l;
+                }
+#pragma unroll
+                for (int nt = 0; nt < 8; nt++) {
+                    sm.u.merge.acc[warp][r][nt * 8 + 2 * tig] = acc[mt][nt][h * 2] * vs_scale;
+                    sm.u.merge.acc[warp][r][nt * 8 + 2 * tig + 1] = acc[mt][nt][h * 2 + 1] * vs_scale;
+                }
+            }
     }
     __syncthreads();
 
-    // ---- per query row: merge the m-tile's warps and the self term ----
-    for (int ri = warp; ri < rows; ri += 4) {
-        const int hh = ri / n, r = ri % n;
-        const int h = g + hh * kv.G;
-        const int w0 = (ri / 16) * WPM;
-        const float ss = sm.s_self[ri];
-        float m = ss;
+    // ---- merge the warps: the CTA's state per row into cm / cl / acc[0] ----
+    for (int ri = warp; ri < rows; ri += NW) {
+        const float fq = sm.fr[ri];
+        float m = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < WPM; w++) m = fmaxf(m, sm.u.merge.m[w0 + w][ri]);
+        for (int w = 0; w < NW; w++) m = fmaxf(m, sm.u.merge.m[w][ri]);
         float l = 0.0f, o0 = 0.0f, o1 = 0.0f;
 #pragma unroll
-        for (int w = 0; w < WPM; w++) {
-            const float mw = sm.u.merge.m[w0 + w][ri];
-            const float f = (mw == -INFINITY) ? 0.0f : __expf(mw - m);
-            l += sm.u.merge.l[w0 + w][ri] * f;
-            o0 += sm.u.merge.acc[w0 + w][ri][lane] * f;
-            o1 += sm.u.merge.acc[w0 + w][ri][lane + 32] * f;
+        for (int w = 0; w < NW; w++) {
+            const float mw = sm.u.merge.m[w][ri];
+            const float f = (mw == -INFINITY) ? 0.0f : ex2((mw - m) * fq);
+            l += sm.u.merge.l[w][ri] * f;
+            o0 += sm.u.merge.acc[w][ri][lane] * f;
+            o1 += sm.u.merge.acc[w][ri][lane + 32] * f;
         }
-        const float ps = __expf(ss - m);
+        __syncwarp();
+        if (lane == 0) {
+            sm.cm[ri] = m;
+            sm.cl[ri] = l;
+        }
+        sm.u.merge.acc[0][ri][lane] = o0;  // this warp alone reads and writes row ri
+        sm.u.merge.acc[0][ri][lane + 32] = o1;
+    }
+
+    // ---- more than one split: publish, and let the last split merge ----
+    const size_t item = (size_t)b * kv.G + g;
+    if (nsplit > 1) {
+        float* part = aw.part + (item * nsplit + split) * QR * PART;
+        for (int ri = warp; ri < rows; ri += NW) {
+            float* pr = part + (size_t)ri * PART;
+            if (lane == 0) {
+                pr[0] = sm.cm[ri];
+                pr[1] = sm.cl[ri];
+            }
+            pr[4 + lane] = sm.u.merge.acc[0][ri][lane];
+            pr[4 + lane + 32] = sm.u.merge.acc[0][ri][lane + 32];
+        }
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) {
+            const int prev = atomicAdd(aw.cnt + item, 1);
+            sm.last = prev == nsplit - 1;
+            if (sm.last) aw.cnt[item] = 0;  // ready for the next launch
+        }
+        __syncthreads();
+        if (!sm.last) return;
+        __threadfence();
+    }
+
+    // ---- final: all splits' states + the self term -> output rows ----
+    __syncwarp();  // (one split) this warp's rows of cm / cl / acc[0] are written
+    for (int ri = warp; ri < rows; ri += NW) {
+        const int hh = ri / n, r = ri % n;
+        const int h = g + hh * kv.G;
+        const float ss = sm.s_self[ri], fq = sm.fr[ri];
+        float m = ss, l, o0, o1;
+        if (nsplit == 1) {
+            const float mc = sm.cm[ri];
+            m = fmaxf(m, mc);
+            const float f = (mc == -INFINITY) ? 0.0f : ex2((mc - m) * fq);
+            l = sm.cl[ri] * f;
+            o0 = sm.u.merge.acc[0][ri][lane] * f;
+            o1 = sm.u.merge.acc[0][ri][lane + 32] * f;
+        } else {
+            const float* part = aw.part + item * nsplit * QR * PART + (size_t)ri * PART;
+            for (int sp2 = 0; sp2 < nsplit; sp2++) m = fmaxf(m, __ldcg(part + (size_t)sp2 * QR * PART));
+            l = 0.0f, o0 = 0.0f, o1 = 0.0f;
+            for (int sp2 = 0; sp2 < nsplit; sp2++) {
+                const float* pr = part + (size_t)sp2 * QR * PART;
+                const float mc = __ldcg(pr);
+                const float f = (mc == -INFINITY) ? 0.0f : ex2((mc - m) * fq);
+                l += __ldcg(pr + 1) * f;
+                o0 += __ldcg(pr + 4 + lane) * f;
+                o1 += __ldcg(pr + 4 + lane + 32) * f;
+            }
+        }
+        const float ps = ex2((ss - m) * fq);
         l += ps;
         o0 += ps * sm.v_self[ri][lane];
         o1 += ps * sm.v_self[ri][lane + 32];
@@ -487,28 +682,43 @@ bool attention_decode_supported(const KvCache& kv, int H, int max_rows) {
     return rows <= QR && kv.S + spec + max_rows - 1 <= 32;
 }
 
+int attention_decode_splits(int nb, int G, int max_splits) {
+    // Split only while the (sequence, kv head) items leave CTA slots (two per
+    // SM) empty: each split repeats the query setup and adds a merge.
+    const int items = std::max(1, nb * G);
+    return std::max(1, std::min(max_splits, (2 * 148) / items));
+}
+
+size_t attention_decode_work_floats(int nb, int G, int nsplit) { return (size_t)nb * G * nsplit * QR * PART; }
+
 template <int MT>
 static pf_status launch_decode(const KvCache& kv, int layer, const RowBatch& rb, const float* qkv, int ldqkv, int k_col,
-                               int v_col, int H, Staged st, SpecPool sp, float* out, int ldo, cudaStream_t stream) {
+                               int v_col, int H, Staged st, SpecPool sp, const AttnWork& aw, float* out, int ldo,
+                               cudaStream_t stream) {
     const int smem = (int)sizeof(AttnSmem<MT>);
     static bool attr = false;
     if (!attr) {
         PF_CUDA(cudaFuncSetAttribute(attn_decode_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         attr = true;
     }
-    dim3 grid(rb.nb, kv.G);
-    attn_decode_kernel<MT><<<grid, 128, smem, stream>>>(kv, layer, rb, qkv, ldqkv, k_col, v_col, H, st, sp, out, ldo,
+    dim3 grid(rb.nb, kv.G, aw.nsplit);
+    attn_decode_kernel<MT><<<grid, 128, smem, stream>>>(kv, layer, rb, qkv, ldqkv, k_col, v_col, H, st, sp, aw, out, ldo,
                                                          device_error_flag());
     return launch_check("attention_decode");
 }
 
 pf_status attention_decode(const KvCache& kv, int layer, const RowBatch& rb, const float* qkv, int ldqkv, int k_col,
-                           int v_col, int H, Staged st, SpecPool sp, float* out, int ldo, cudaStream_t stream) {
+                           int v_col, int H, Staged st, SpecPool sp, const AttnWork& aw, float* out, int ldo,
+                           cudaStream_t stream) {
     PF_CHECK(kv.hd == 64, "attention_decode: head_dim must be 64");
     PF_CHECK(attention_decode_supported(kv, H, rb.max_rows), "attention_decode: too many query rows");
+    PF_CHECK(aw.nsplit >= 1 && aw.nsplit <= 65535, "attention_decode: bad split count");
+    PF_CHECK(aw.nsplit == 1 || (aw.part && aw.cnt && aw.part_floats >= attention_decode_work_floats(rb.nb, kv.G, aw.nsplit) &&
+                                aw.cnt_elems >= (size_t)rb.nb * kv.G),
+             "attention_decode: workspace too small for %d splits", aw.nsplit);
     if ((H / kv.G) * rb.max_rows <= 16)
-        return launch_decode<1>(kv, layer, rb, qkv, ldqkv, k_col, v_col, H, st, sp, out, ldo, stream);
-    return launch_decode<2>(kv, layer, rb, qkv, ldqkv, k_col, v_col, H, st, sp, out, ldo, stream);
+        return launch_decode<1>(kv, layer, rb, qkv, ldqkv, k_col, v_col, H, st, sp, aw, out, ldo, stream);
+    return launch_decode<2>(kv, layer, rb, qkv, ldqkv, k_col, v_col, H, st, sp, aw, out, ldo, stream);
 }
 
 }  // namespace pf

@@ -112,6 +112,12 @@ struct pf_engine {
     // [splits][M][d], summed by resid_rmsnorm_quant.
     int32_t* rws = nullptr;
     size_t rws_elems = 0;
+    // Split-context attention: partial softmax states and arrival counters.
+    static constexpr int kMaxAttnSplits = 8;
+    int attn_splits = 0;  // 0: automatic
+    float* attn_part = nullptr;
+    int* attn_cnt = nullptr;
+    size_t attn_part_floats = 0, attn_cnt_elems = 0;
 
     pf_sampling_config samp{0.8f, 0.95f, 40, 1};
     std::vector<std::mt19937> rngs;
@@ -252,8 +258,15 @@ struct pf_engine {
             PF_TRY(kv_quant_rows(qkv, NQKV, NQ, NQ + NK, M, nullptr, G, hd, sl, st));
             if (evicting) PF_TRY(kv_pool_spec(kv, l, rb, sp, st));
             PF_TRY(tbegin(0));
-            if (attention_decode_supported(kv, H, rb.max_rows))
-                PF_TRY(attention_decode(kv, l, rb, qkv, NQKV, NQ, NQ + NK, H, sl, sp, att, NQ, st));
+            if (attention_decode_supported(kv, H, rb.max_rows)) {
+                AttnWork aw;
+                aw.nsplit = attn_splits > 0 ? attn_splits : attention_decode_splits(rb.nb, G, kMaxAttnSplits);
+                aw.part = attn_part;
+                aw.part_floats = attn_part_floats;
+                aw.cnt = attn_cnt;
+                aw.cnt_elems = attn_cnt_elems;
+                PF_TRY(attention_decode(kv, l, rb, qkv, NQKV, NQ, NQ + NK, H, sl, sp, aw, att, NQ, st));
+            }
             else
                 PF_TRY(attention(kv, l, rb, qkv, NQKV, NQ, NQ + NK, H, sl, sp, att, NQ, st));
             PF_TRY(tend());
@@ -617,6 +630,11 @@ pf_status pf_engine_create(const pf_model_config* c, int32_t max_seqs, int32_t m
     for (int m = 1; m <= e->Mcap; m++)  // slices of the K-split residual projections, any row count
         e->rws_elems = std::max(e->rws_elems, (size_t)std::max(gemm_tc_slices(m, d, e->NQ), gemm_tc_slices(m, d, F)) * m * d);
     E_TRY(dalloc(&e->rws, e->rws_elems, o));
+    e->attn_part_floats = attention_decode_work_floats(max_seqs, G, pf_engine::kMaxAttnSplits);
+    e->attn_cnt_elems = (size_t)max_seqs * G;
+    E_TRY(dalloc(&e->attn_part, e->attn_part_floats, o));
+    E_TRY(dalloc(&e->attn_cnt, e->attn_cnt_elems, o));
+    if (cudaMemset(e->attn_cnt, 0, e->attn_cnt_elems * sizeof(int)) != cudaSuccess) return fail(PF_ERR_CUDA);
     e->gcnt_elems = 296;
     E_TRY(dalloc(&e->gcnt, e->gcnt_elems, o));
     PF_CUDA(cudaMemset(e->gws, 0, e->gws_elems * 4));
@@ -1117,6 +1135,14 @@ pf_status pf_engine_launches_per_step(pf_engine* e, int32_t* kernels) {
 pf_status pf_engine_last_ms(pf_engine* e, float* ms) {
     PF_CHECK(e && ms, "pf_engine_last_ms: null argument");
     *ms = e->last_ms;
+    return PF_OK;
+}
+
+pf_status pf_engine_set_attention_splits(pf_engine* e, int32_t n) {
+    PF_CHECK(e, "pf_engine_set_attention_splits: null engine");
+    PF_CHECK(n >= 0 && n <= pf_engine::kMaxAttnSplits, "attention splits must be 0..%d", pf_engine::kMaxAttnSplits);
+    if (n != e->attn_splits) e->graph_dirty = true;
+    e->attn_splits = n;
     return PF_OK;
 }
 

@@ -79,9 +79,22 @@ pf_status attention(const KvCache& kv, int layer, const RowBatch& rb, const floa
                     int v_col, int H, Staged st, SpecPool sp, float* out, int ldo, cudaStream_t stream);
 // Tensor-core variant for batches of at most 32 / (H/G) rows per sequence
 // whose sink, in-batch pool entries and earlier rows fit one 32-entry block.
+// The context of each (sequence, kv head) is split over `nsplit` CTAs whose
+// partial softmax states meet in `part`; `cnt` ([nb][G] ints, zero before the
+// first launch) counts the arrivals and is left zero.
+struct AttnWork {
+    int nsplit = 1;
+    float* part = nullptr;
+    size_t part_floats = 0;
+    int* cnt = nullptr;
+    size_t cnt_elems = 0;
+};
 bool attention_decode_supported(const KvCache& kv, int H, int max_rows);
+int attention_decode_splits(int nb, int G, int max_splits);
+size_t attention_decode_work_floats(int nb, int G, int nsplit);
 pf_status attention_decode(const KvCache& kv, int layer, const RowBatch& rb, const float* qkv, int ldqkv, int k_col,
-                           int v_col, int H, Staged st, SpecPool sp, float* out, int ldo, cudaStream_t stream);
+                           int v_col, int H, Staged st, SpecPool sp, const AttnWork& aw, float* out, int ldo,
+                           cudaStream_t stream);
 // Commits rows [0, n_commit[b]) of every sequence into the cache, all layers.
 // `staged` holds layer 0; layer l is at +l*M*G*hd (int8) and +l*M*G (scales).
 pf_status kv_commit(const KvCache& kv, const RowBatch& rb, const int* n_commit, Staged staged, int M_stride,

@@ -25,8 +25,9 @@ def need_device():
         pytest.skip("no sm_100 device")
 
 
-def gpu_engine(cfg: Cfg, w, max_seqs, max_pos, sampling=None, skip_threshold=None):
+def gpu_engine(cfg: Cfg, w, max_seqs, max_pos, sampling=None, skip_threshold=None, attn_splits=0):
     e = pf.BatchEngine(cfg.product(), max_seqs, max_pos)
+    e.set_attention_splits(attn_splits)
     for l in range(cfg.n_layers):
         for m in range(7):
             a, rs = w[(l, m)]
@@ -68,9 +69,11 @@ def compare_step_state(g, o, check_kv=True):
     np.testing.assert_array_equal(g.read_drafts()[finite], o.drafts()[finite])
 
 
-def run_pair(cfg, w, prm, steps, max_pos=None, forced=None, sampling=None, seeds=None, skip_threshold=None):
+def run_pair(cfg, w, prm, steps, max_pos=None, forced=None, sampling=None, seeds=None, skip_threshold=None,
+             attn_splits=0):
     max_pos = max_pos or (max(len(x) for x in prm) + (steps + 1) * (cfg.n_mtp_heads + 1) + 8)
-    g = gpu_engine(cfg, w, len(prm), max_pos, sampling=sampling, skip_threshold=skip_threshold)
+    g = gpu_engine(cfg, w, len(prm), max_pos, sampling=sampling, skip_threshold=skip_threshold,
+                   attn_splits=attn_splits)
     o = OracleEngine(cfg, w, order=1, sampling=sampling, skip_threshold=skip_threshold)
     g.prefill(prm, seeds)
     o.prefill(prm, seeds)
@@ -92,8 +95,14 @@ def run_pair(cfg, w, prm, steps, max_pos=None, forced=None, sampling=None, seeds
     return g, o
 
 
-def compare_kv(g, o, cfg, n_seqs):
+def compare_kv(g, o, cfg, n_seqs, scale_frac=1.0):
+    """int8 bytes identical for >= 99.9%; K/V scales within RTOL for at least
+    `scale_frac` of the entries and within 2% for all.  (Over long contexts a
+    float difference of ~1e-7 upstream occasionally moves an int8 activation
+    across a rounding boundary; one step of 1/127 moves that entry's K/V row,
+    and its scale, by up to a few tenths of a percent.)"""
     tot = same = 0
+    n_sc = ok_sc = 0
     for b in range(n_seqs):
         for l in range(cfg.n_layers):
             for h in range(cfg.n_kv_heads):
@@ -102,9 +111,13 @@ def compare_kv(g, o, cfg, n_seqs):
                 assert len(gk) == len(ok)
                 tot += gk.size * 2
                 same += int((gk == ok).sum() + (gv == ov).sum())
-                np.testing.assert_allclose(gks, oks, rtol=RTOL)
-                np.testing.assert_allclose(gvs, ovs, rtol=RTOL)
+                for a, w in ((gks, oks), (gvs, ovs)):
+                    rel = np.abs(a - w) / np.maximum(np.abs(w), 1e-30)
+                    assert rel.max() < 0.02, rel.max()
+                    n_sc += rel.size
+                    ok_sc += int((rel <= RTOL).sum())
     assert same / tot >= 0.999, same / tot
+    assert ok_sc >= scale_frac * n_sc, (ok_sc, n_sc)
 
 
 @pytest.fixture(scope="module")
@@ -161,6 +174,19 @@ def test_gqa_and_eviction_pooling():
     prm = prompts(2, [40, 23], cfg.n_vocab, seed=4)
     g, o = run_pair(cfg, w, prm, 8)
     compare_kv(g, o, cfg, 2)
+
+
+@pytest.mark.parametrize("splits", [0, 1, 3])
+def test_long_context_matches_oracle(splits):
+    """Contexts of 1-2k entries: many 32-entry blocks per (sequence, kv head),
+    split over 1, 3 or (automatic) 8 CTAs, pool blocks and a partly filled
+    window ring."""
+    cfg = Cfg(n_heads=4, n_kv_heads=2, n_embd=256, window_size=1024, pool_block=16, max_context=4096,
+              n_mtp_heads=2)
+    w = make_weights(cfg, seed=5)
+    prm = prompts(3, [1500, 700, 1100], cfg.n_vocab, seed=10)
+    g, o = run_pair(cfg, w, prm, 4, attn_splits=splits)
+    compare_kv(g, o, cfg, 3, scale_frac=0.995)
 
 
 def test_layer_skip_matches_oracle():
