@@ -48,6 +48,7 @@ __device__ __forceinline__ void quant64_warp(float a, float b, int8_t& qa, int8_
 // ---------------------------------------------------------------------------
 __global__ void kv_quant_kernel(const float* __restrict__ qkv, int ld, int k_col, int v_col, int M,
                                 const int* m_dev, int G, Staged st) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the attention may start streaming the cache
     const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     const int m_act = m_dev ? min(M, *m_dev) : M;
@@ -81,6 +82,7 @@ pf_status kv_quant_rows(const float* qkv, int ldqkv, int k_col, int v_col, int M
 // requantized.  All evicted entries involved are committed ring entries.
 // ---------------------------------------------------------------------------
 __global__ void kv_pool_spec_kernel(KvCache kv, int layer, RowBatch rb, SpecPool sp) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the attention may start streaming the cache
     const int b = blockIdx.x, g = blockIdx.y, d = threadIdx.x;  // 64 threads
     const int n = rb.n[b];
     if (n == 0) return;

@@ -93,9 +93,12 @@ constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
 constexpr int kMagicBits = 0x4B400000;
 __device__ __forceinline__ float i2f_small(int32_t a) { return __fsub_rn(__int_as_float(a + kMagicBits), kMagic); }
 
+// a + b/254 + c/254^2 from the three planes' exact sums: b*254 + c is exact
+// in int32 (|b| <= 64*127*127); its conversion rounds only the second-order
+// part, and one fused multiply-add rounds the result.
 __device__ __forceinline__ float comb(int32_t a, int32_t b, int32_t c) {
-    const float r = 1.0f / 254.0f;
-    return i2f_small(a) + (i2f_small(b) + i2f_small(c) * r) * r;
+    const float r2 = 1.0f / (254.0f * 254.0f);
+    return __fmaf_rn(__int2float_rn(b * 254 + c), r2, i2f_small(a));
 }
 
 __device__ __forceinline__ void digits3(float x, float mul, int& d1, int& d2, int& d3) {
@@ -253,6 +256,10 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
         load_block(i);
         cp_commit();
     }
+    // The committed cache streamed above was written by earlier steps; the
+    // queries, staged rows and in-batch pool entries below come from the
+    // kernels just before this one (programmatic dependent launch).
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     // ---- the extra block: sink entries, pool entries finalized inside the
     // batch (visible from the row that finalizes them), staged earlier rows.
@@ -411,12 +418,15 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
 
         // ---- v-scale reference: a power of two per warp, raised when a block's
         // scales outgrow it (the accumulators are rescaled exactly) ----
-        const float vmax = warp_max(valid ? bb.vs[lane] : 0.0f);
-        if (vmax > 0.0f && vmax <= 3.0e38f) {
-            const int ev = exp_of(vmax);
+        const float vl = valid ? bb.vs[lane] : 0.0f;
+        // (a warp-wide maximum only for the first block and when some scale
+        // leaves the range of the reference)
+        if (__any_sync(0xffffffffu, have_ref ? !(vl < pow2i(min(126, eref + 4))) : vl > 0.0f)) {
+            const float vmax = warp_max(vl);
+            const int ev = (vmax > 0.0f && vmax <= 3.0e38f) ? exp_of(vmax) : (have_ref ? eref : 0);
             if (!have_ref) {
                 eref = ev;
-                have_ref = true;
+                have_ref = vmax > 0.0f && vmax <= 3.0e38f;
             } else if (ev > eref + 4) {
                 const float c = pow2i(max(eref - ev, -126));
 #pragma unroll
@@ -530,7 +540,8 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
                 for (int c = 0; c < 4; c++) {
                     const int h = c >> 1;
                     const float sv = s[mt][j][c];
-                    const float p = (sv == -INFINITY) ? 0.0f : ex2((sv - mref[mt][h]) * fr[mt][h]);
+                    // every entry of a full block is visible and finite
+                    const float p = (!full && sv == -INFINITY) ? 0.0f : ex2((sv - mref[mt][h]) * fr[mt][h]);
                     lsum[mt][h] += p;
                     w[c] = p * vsn[2 * j + (c & 1)];
                 }
@@ -701,9 +712,18 @@ static pf_status launch_decode(const KvCache& kv, int layer, const RowBatch& rb,
         PF_CUDA(cudaFuncSetAttribute(attn_decode_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         attr = true;
     }
-    dim3 grid(rb.nb, kv.G, aw.nsplit);
-    attn_decode_kernel<MT><<<grid, 128, smem, stream>>>(kv, layer, rb, qkv, ldqkv, k_col, v_col, H, st, sp, aw, out, ldo,
-                                                         device_error_flag());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(rb.nb, kv.G, aw.nsplit);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    PF_CUDA(cudaLaunchKernelEx(&cfg, attn_decode_kernel<MT>, kv, layer, rb, qkv, ldqkv, k_col, v_col, H, st, sp, aw, out,
+                               ldo, device_error_flag()));
     return launch_check("attention_decode");
 }
 
