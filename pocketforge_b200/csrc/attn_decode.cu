@@ -178,7 +178,7 @@ struct __align__(16) BlockBuf {
 
 template <int MT>
 struct __align__(16) AttnSmem {
-    int8_t qd[3][16 * MT][64];  // query digit planes
+    uint4 qf[MT][3][2][32];  // query digit planes as A fragments [m-tile][plane][k-step][lane]
     float fr[QR];            // per row: f = s * log2(e) / 8 (0 for padding rows)
     float s_self[QR];        // self-term score, raw units
     float v_self[QR][64];    // self-term values
@@ -334,12 +334,21 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
         int a1, a2, a3, b1, b2, b3;
         digits3(x0, mul, a1, a2, a3);
         digits3(x1, mul, b1, b2, b3);
-        sm.qd[0][ri][lane] = (int8_t)a1;
-        sm.qd[1][ri][lane] = (int8_t)a2;
-        sm.qd[2][ri][lane] = (int8_t)a3;
-        sm.qd[0][ri][lane + 32] = (int8_t)b1;
-        sm.qd[1][ri][lane + 32] = (int8_t)b2;
-        sm.qd[2][ri][lane + 32] = (int8_t)b3;
+        // byte d of row ri -> fragment (m-tile, plane, k-step, lane g*4 + t), register
+        // 2*((w>>2)&1) + (row >= 8 within the tile), byte w & 3, with t = d/16, w = d%16
+        {
+            int8_t* qb8 = reinterpret_cast<int8_t*>(&sm.qf[0][0][0][0]);
+            const int mt = ri >> 4, g8 = ri & 7, h8 = (ri >> 3) & 1;
+#pragma unroll
+            for (int half = 0; half < 2; half++) {
+                const int d = lane + 32 * half, t = d >> 4, w = d & 15;
+                const int reg = ((w >> 2) & 1) * 2 + h8;
+                const size_t base = (((size_t)mt * 3 * 2 + (w >> 3)) * 32 + g8 * 4 + t) * 16 + reg * 4 + (w & 3);
+                const int dd[3] = {half ? b1 : a1, half ? b2 : a2, half ? b3 : a3};
+#pragma unroll
+                for (int p = 0; p < 3; p++) qb8[base + (size_t)p * 2 * 32 * 16] = (int8_t)dd[p];
+            }
+        }
         // self term with the float k and v (src/engine.cpp:760-778), in raw
         // units: (q . k) / sqrt(64) / (s / sqrt(64))
         const float sc = warp_sum(x0 * kx[k][0] + x1 * kx[k][1]) * mul;
@@ -466,11 +475,11 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
         float s[MT][4][4];
 #pragma unroll
         for (int mt = 0; mt < MT; mt++) {
-            uint4 qa[3], qb[3];
+            uint4 qa[3], qb[3];  // k-step 0 / 1 A fragments of each plane
 #pragma unroll
             for (int p = 0; p < 3; p++) {
-                qa[p] = *reinterpret_cast<const uint4*>(&sm.qd[p][mt * 16 + gid][16 * tig]);
-                qb[p] = *reinterpret_cast<const uint4*>(&sm.qd[p][mt * 16 + gid + 8][16 * tig]);
+                qa[p] = sm.qf[mt][p][0][lane];
+                qb[p] = sm.qf[mt][p][1][lane];
             }
 #pragma unroll
             for (int j = 0; j < 4; j++) {
@@ -479,8 +488,8 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
 #pragma unroll
                 for (int p = 0; p < 3; p++) {
                     ac[p][0] = ac[p][1] = ac[p][2] = ac[p][3] = 0;
-                    mma_s8(ac[p], qa[p].x, qb[p].x, qa[p].y, qb[p].y, kf.x, kf.y);
-                    mma_s8(ac[p], qa[p].z, qb[p].z, qa[p].w, qb[p].w, kf.z, kf.w);
+                    mma_s8(ac[p], qa[p].x, qa[p].y, qa[p].z, qa[p].w, kf.x, kf.y);
+                    mma_s8(ac[p], qb[p].x, qb[p].y, qb[p].z, qb[p].w, kf.z, kf.w);
                 }
 #pragma unroll
                 for (int c = 0; c < 4; c++) {
