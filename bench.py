@@ -201,7 +201,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--seqs", type=int, default=0, help="override sequences per GPU")
+    ap.add_argument("--seqs", type=int, default=0, help="override sequences per GPU (global with --strong)")
+    ap.add_argument("--strong", action="store_true",
+                    help="strong scaling: the config's sequences are the global batch, split over the GPUs")
     ap.add_argument("--prompt", type=int, default=0, help="override prompt length")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -228,7 +230,12 @@ def main():
                                 device_id=torch.device("cuda", local))
     preset = pf.PRESETS[args.config]
     model = preset["model"]
-    seqs = args.seqs or preset["seqs"]
+    global_seqs = (args.seqs or preset["seqs"]) * (1 if args.strong else world)
+    # Weak scaling: every rank owns the config's sequences of a global batch of
+    # seqs * world; strong scaling: the config's batch is split over the ranks.
+    # Rank r holds the contiguous block [g0, g1) of global ids.
+    g0, g1 = replicas.sequence_slice(global_seqs, world, rank)
+    seqs = g1 - g0
     plen = args.prompt or preset["prompt"]
     K = model.n_mtp_heads
     R = K + 1
@@ -240,9 +247,6 @@ def main():
     sampling = preset.get("sampling")
     if sampling:
         eng.set_sampling(sampling["temperature"], sampling["top_p"], sampling["top_k"], False)
-    # Weak scaling: every rank owns `seqs` sequences of a global batch of
-    # seqs * world; rank r holds the contiguous block of global ids below.
-    g0, g1 = replicas.sequence_slice(seqs * world, world, rank)
     prompts = make_prompts(range(g0, g1), plen, model.n_vocab)
     seeds = [sampling["seed"] + i for i in range(g0, g1)] if sampling else None
 
@@ -319,12 +323,13 @@ def main():
         line = {
             "metric": METRIC, "value": tokens_all / (ms_max * 1e-3), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "higher_is_better": True, "scaling": "strong" if args.strong else "weak", "vs_baseline": None,
+            "dtype": "int8",
             "data": "synthetic",
             "config": {"workload": f"{args.config}: {seqs} sequences/GPU x {plen}-token uniform-random prompts, "
                                    f"MTP K={K} {'stochastic' if sampling else 'greedy'} verify of M={seqs * R} "
                                    f"rows/step, 1B Q4 model (22L, d2048, 32/8 heads, ffn 5632, vocab 16384)",
-                       "seqs_per_gpu": seqs, "global_seqs": seqs * world, "prompt": plen,
+                       "seqs_per_gpu": seqs, "global_seqs": global_seqs, "prompt": plen,
                        "context_avg": ctx_avg, "window": model.window_size,
                        "l2": "no flush: weights (0.52 GB) + KV read per step exceed the 126 MB L2",
                        "parallelism": f"replicas x{world}"},
