@@ -51,6 +51,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "kv.cuh"
 
@@ -232,10 +233,10 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
     const int b_end = (int)((int64_t)nblk * (split + 1) / nsplit);
 
     // ---- this warp's cp.async ring: block of iteration i is b_begin + warp + NW * i ----
-    auto load_block = [&](int i) {
+    auto load_block = [&](int i, int slot) {
         const int blk = b_begin + warp + NW * i;
         if (blk >= b_end || blk >= nkv) return;
-        BlockBuf& bb = sm.u.ring[warp][i % NSW];
+        BlockBuf& bb = sm.u.ring[warp][slot];
         const bool is_pool = blk < pool_blocks;
         const int bi = is_pool ? blk : blk - pool_blocks;
         const size_t e0 = (is_pool ? u * kv.P_pad : u * kv.W_pad) + (size_t)bi * 32;
@@ -253,7 +254,7 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
     };
 #pragma unroll
     for (int i = 0; i < NSW - 1; i++) {
-        load_block(i);
+        load_block(i, i);
         cp_commit();
     }
     // The committed cache streamed above was written by earlier steps; the
@@ -398,15 +399,17 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
     int eref = 0;
     bool have_ref = false;
 
+    int slot = 0;  // ring slot of block i (i % NSW)
     for (int i = 0;; i++) {
         const int blk = b_begin + warp + NW * i;
         if (blk >= b_end) break;
         cp_wait<NSW - 2>();
-        __syncwarp();  // every lane's copies of block i landed; stage (i - 1) % NSW is free
-        load_block(i + NSW - 1);
+        __syncwarp();  // every lane's copies of block i landed; slot (i - 1) % NSW is free
+        load_block(i + NSW - 1, slot == 0 ? NSW - 1 : slot - 1);
         cp_commit();
         const bool is_ex = blk == nkv;
-        const BlockBuf& bb = is_ex ? sm.ex : sm.u.ring[warp][i % NSW];
+        const BlockBuf& bb = is_ex ? sm.ex : sm.u.ring[warp][slot];
+        slot = (slot + 1 == NSW) ? 0 : slot + 1;
 
         // ---- visibility of entry `lane`: query rows [lo, hi] of the sequence ----
         int lo = BIG, hi = -1;
@@ -449,140 +452,149 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
         }
         const float vmul = pow2i(-max(-126, min(126, eref)));
 
-        // ---- this thread's entries e = 8j + 2*tig + cc: scales (and masks) ----
-        float ksv[8], vsn[8];
-        int lo8[8], hi8[8];
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const float2 k2 = *reinterpret_cast<const float2*>(&bb.ks[8 * j + 2 * tig]);
-            const float2 v2 = *reinterpret_cast<const float2*>(&bb.vs[8 * j + 2 * tig]);
-            ksv[2 * j] = k2.x;
-            ksv[2 * j + 1] = k2.y;
-            vsn[2 * j] = v2.x * vmul;
-            vsn[2 * j + 1] = v2.y * vmul;
-        }
-        if (!full) {
-#pragma unroll
-            for (int k = 0; k < 8; k++) {
-                const int e = 8 * (k >> 1) + 2 * tig + (k & 1);
-                lo8[k] = __shfl_sync(0xffffffffu, lo, e);
-                hi8[k] = __shfl_sync(0xffffffffu, hi, e);
-                if (!(hi8[k] >= 0 && lo8[k] < BIG)) vsn[k] = 0.0f;  // a masked entry must not bring a NaN scale in
-            }
-        }
-
-        // ---- scores: S = Q . K^T (three digit planes, exact int32), s_raw = S * k_scale ----
-        float s[MT][4][4];
-#pragma unroll
-        for (int mt = 0; mt < MT; mt++) {
-            uint4 qa[3], qb[3];  // k-step 0 / 1 A fragments of each plane
-#pragma unroll
-            for (int p = 0; p < 3; p++) {
-                qa[p] = sm.qf[mt][p][0][lane];
-                qb[p] = sm.qf[mt][p][1][lane];
-            }
+        // The rest of the block's work, specialised for blocks whose entries
+        // every row sees (no masks) and for the others.
+        auto body = [&](auto full_tag) {
+            constexpr bool FULL = decltype(full_tag)::value;
+            // ---- this thread's entries e = 8j + 2*tig + cc: scales (and masks) ----
+            float ksv[8], vsn[8];
+            int lo8[8], hi8[8];
 #pragma unroll
             for (int j = 0; j < 4; j++) {
-                const uint4 kf = *reinterpret_cast<const uint4*>(&bb.k[8 * j + gid][16 * tig]);
-                int32_t ac[3][4];
+                const float2 k2 = *reinterpret_cast<const float2*>(&bb.ks[8 * j + 2 * tig]);
+                const float2 v2 = *reinterpret_cast<const float2*>(&bb.vs[8 * j + 2 * tig]);
+                ksv[2 * j] = k2.x;
+                ksv[2 * j + 1] = k2.y;
+                vsn[2 * j] = v2.x * vmul;
+                vsn[2 * j + 1] = v2.y * vmul;
+            }
+            if (!FULL) {
+#pragma unroll
+                for (int k = 0; k < 8; k++) {
+                    const int e = 8 * (k >> 1) + 2 * tig + (k & 1);
+                    lo8[k] = __shfl_sync(0xffffffffu, lo, e);
+                    hi8[k] = __shfl_sync(0xffffffffu, hi, e);
+                    if (!(hi8[k] >= 0 && lo8[k] < BIG)) vsn[k] = 0.0f;  // a masked entry must not bring a NaN scale in
+                }
+            }
+
+            // ---- scores: S = Q . K^T (three digit planes, exact int32), s_raw = S * k_scale ----
+            float s[MT][4][4];
+#pragma unroll
+            for (int mt = 0; mt < MT; mt++) {
+                uint4 qa[3], qb[3];  // k-step 0 / 1 A fragments of each plane
 #pragma unroll
                 for (int p = 0; p < 3; p++) {
-                    ac[p][0] = ac[p][1] = ac[p][2] = ac[p][3] = 0;
-                    mma_s8(ac[p], qa[p].x, qa[p].y, qa[p].z, qa[p].w, kf.x, kf.y);
-                    mma_s8(ac[p], qb[p].x, qb[p].y, qb[p].z, qb[p].w, kf.z, kf.w);
+                    qa[p] = sm.qf[mt][p][0][lane];
+                    qb[p] = sm.qf[mt][p][1][lane];
                 }
 #pragma unroll
-                for (int c = 0; c < 4; c++) {
-                    const int k = 2 * j + (c & 1);
-                    float v = comb(ac[0][c], ac[1][c], ac[2][c]) * ksv[k];
-                    if (!full) {
-                        const int r = rr[mt][c >> 1];
-                        if (!(r >= lo8[k] && r <= hi8[k])) v = -INFINITY;
+                for (int j = 0; j < 4; j++) {
+                    const uint4 kf = *reinterpret_cast<const uint4*>(&bb.k[8 * j + gid][16 * tig]);
+                    int32_t ac[3][4];
+#pragma unroll
+                    for (int p = 0; p < 3; p++) {
+                        ac[p][0] = ac[p][1] = ac[p][2] = ac[p][3] = 0;
+                        mma_s8(ac[p], qa[p].x, qa[p].y, qa[p].z, qa[p].w, kf.x, kf.y);
+                        mma_s8(ac[p], qb[p].x, qb[p].y, qb[p].z, qb[p].w, kf.z, kf.w);
                     }
-                    s[mt][j][c] = v;
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        const int k = 2 * j + (c & 1);
+                        float v = comb(ac[0][c], ac[1][c], ac[2][c]) * ksv[k];
+                        if (!FULL) {
+                            const int r = rr[mt][c >> 1];
+                            if (!(r >= lo8[k] && r <= hi8[k])) v = -INFINITY;
+                        }
+                        s[mt][j][c] = v;
+                    }
                 }
             }
-        }
 
-        // ---- online softmax with a lazily raised reference maximum ----
-        float bmax[MT][2];
-        bool need = false;
-#pragma unroll
-        for (int mt = 0; mt < MT; mt++)
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-                float bm = -INFINITY;
-#pragma unroll
-                for (int j = 0; j < 4; j++) bm = fmaxf(bm, fmaxf(s[mt][j][2 * h], s[mt][j][2 * h + 1]));
-                bm = quad_max(bm);
-                bmax[mt][h] = bm;
-                const float m = mref[mt][h];
-                need |= (bm > -INFINITY) && (m == -INFINITY || (bm - m) * fr[mt][h] > kMaxLead);
-            }
-        if (__any_sync(0xffffffffu, need)) {
+            // ---- online softmax with a lazily raised reference maximum ----
+            float bmax[MT][2];
+            bool need = false;
 #pragma unroll
             for (int mt = 0; mt < MT; mt++)
 #pragma unroll
                 for (int h = 0; h < 2; h++) {
+                    float bm = -INFINITY;
+#pragma unroll
+                    for (int j = 0; j < 4; j++) bm = fmaxf(bm, fmaxf(s[mt][j][2 * h], s[mt][j][2 * h + 1]));
+                    bm = quad_max(bm);
+                    bmax[mt][h] = bm;
                     const float m = mref[mt][h];
-                    const float mn = fmaxf(m, bmax[mt][h]);
-                    if (mn > m) {
-                        const float corr = (m == -INFINITY) ? 0.0f : ex2((m - mn) * fr[mt][h]);
-                        lsum[mt][h] *= corr;
+                    need |= (bm > -INFINITY) && (m == -INFINITY || (bm - m) * fr[mt][h] > kMaxLead);
+                }
+            if (__any_sync(0xffffffffu, need)) {
 #pragma unroll
-                        for (int nt = 0; nt < 8; nt++) {
-                            acc[mt][nt][2 * h] *= corr;
-                            acc[mt][nt][2 * h + 1] *= corr;
+                for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        const float m = mref[mt][h];
+                        const float mn = fmaxf(m, bmax[mt][h]);
+                        if (mn > m) {
+                            const float corr = (m == -INFINITY) ? 0.0f : ex2((m - mn) * fr[mt][h]);
+                            lsum[mt][h] *= corr;
+#pragma unroll
+                            for (int nt = 0; nt < 8; nt++) {
+                                acc[mt][nt][2 * h] *= corr;
+                                acc[mt][nt][2 * h + 1] *= corr;
+                            }
+                            mref[mt][h] = mn;
                         }
-                        mref[mt][h] = mn;
                     }
-                }
-        }
-        // p = 2^((s_raw - m) f), w = p * v_scale / 2^E -> two fp16 planes (A fragments)
-        uint32_t wa[MT][2][2][4];  // [m-tile][k-step][plane][reg]
-#pragma unroll
-        for (int mt = 0; mt < MT; mt++) {
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                float w[4];
-#pragma unroll
-                for (int c = 0; c < 4; c++) {
-                    const int h = c >> 1;
-                    const float sv = s[mt][j][c];
-                    // every entry of a full block is visible and finite
-                    const float p = (!full && sv == -INFINITY) ? 0.0f : ex2((sv - mref[mt][h]) * fr[mt][h]);
-                    lsum[mt][h] += p;
-                    w[c] = p * vsn[2 * j + (c & 1)];
-                }
-                const float h0 = trunc11(w[0]), h1 = trunc11(w[1]), h2 = trunc11(w[2]), h3 = trunc11(w[3]);
-                const int ks = j >> 1, r0 = (j & 1) * 2;  // tiles 2s / 2s+1 -> a0,a1 / a2,a3
-                wa[mt][ks][0][r0] = pack_h2(h0, h1);
-                wa[mt][ks][0][r0 + 1] = pack_h2(h2, h3);
-                wa[mt][ks][1][r0] = pack_h2(w[0] - h0, w[1] - h1);
-                wa[mt][ks][1][r0 + 1] = pack_h2(w[2] - h2, w[3] - h3);
             }
-        }
-
-        // ---- O += W . V ----
-#pragma unroll
-        for (int nt = 0; nt < 8; nt++) {
-            const uint2 vf = *reinterpret_cast<const uint2*>(&bb.v[(nt * 8 + gid) * 32 + 8 * tig]);
-            uint32_t vb[2][2];
-            i8x4_to_h2(vf.x, vb[0][0], vb[0][1]);
-            i8x4_to_h2(vf.y, vb[1][0], vb[1][1]);
+            // p = 2^((s_raw - m) f), w = p * v_scale / 2^E -> two fp16 planes (A fragments)
+            uint32_t wa[MT][2][2][4];  // [m-tile][k-step][plane][reg]
 #pragma unroll
             for (int mt = 0; mt < MT; mt++) {
-                float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-                for (int p = 1; p >= 0; p--)  // the remainder plane first
+                for (int j = 0; j < 4; j++) {
+                    float w[4];
 #pragma unroll
-                    for (int ks = 0; ks < 2; ks++)
-                        mma_f16(o, wa[mt][ks][p][0], wa[mt][ks][p][1], wa[mt][ks][p][2], wa[mt][ks][p][3], vb[ks][0],
-                                vb[ks][1]);
-#pragma unroll
-                for (int c = 0; c < 4; c++) acc[mt][nt][c] += o[c];
+                    for (int c = 0; c < 4; c++) {
+                        const int h = c >> 1;
+                        const float sv = s[mt][j][c];
+                        // every entry of a FULL block is visible and finite
+                        const float p = (!FULL && sv == -INFINITY) ? 0.0f : ex2((sv - mref[mt][h]) * fr[mt][h]);
+                        lsum[mt][h] += p;
+                        w[c] = p * vsn[2 * j + (c & 1)];
+                    }
+                    const float h0 = trunc11(w[0]), h1 = trunc11(w[1]), h2 = trunc11(w[2]), h3 = trunc11(w[3]);
+                    const int ks = j >> 1, r0 = (j & 1) * 2;  // tiles 2s / 2s+1 -> a0,a1 / a2,a3
+                    wa[mt][ks][0][r0] = pack_h2(h0, h1);
+                    wa[mt][ks][0][r0 + 1] = pack_h2(h2, h3);
+                    wa[mt][ks][1][r0] = pack_h2(w[0] - h0, w[1] - h1);
+                    wa[mt][ks][1][r0 + 1] = pack_h2(w[2] - h2, w[3] - h3);
+                }
             }
-        }
+
+            // ---- O += W . V ----
+#pragma unroll
+            for (int nt = 0; nt < 8; nt++) {
+                const uint2 vf = *reinterpret_cast<const uint2*>(&bb.v[(nt * 8 + gid) * 32 + 8 * tig]);
+                uint32_t vb[2][2];
+                i8x4_to_h2(vf.x, vb[0][0], vb[0][1]);
+                i8x4_to_h2(vf.y, vb[1][0], vb[1][1]);
+#pragma unroll
+                for (int mt = 0; mt < MT; mt++) {
+                    float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                    for (int p = 1; p >= 0; p--)  // the remainder plane first
+#pragma unroll
+                        for (int ks = 0; ks < 2; ks++)
+                            mma_f16(o, wa[mt][ks][p][0], wa[mt][ks][p][1], wa[mt][ks][p][2], wa[mt][ks][p][3], vb[ks][0],
+                                    vb[ks][1]);
+#pragma unroll
+                    for (int c = 0; c < 4; c++) acc[mt][nt][c] += o[c];
+                }
+            }
+        };
+        if (full)
+            body(std::true_type{});
+        else
+            body(std::false_type{});
     }
     cp_wait<0>();
     __syncthreads();  // every warp left its ring: the ring area becomes the merge area
