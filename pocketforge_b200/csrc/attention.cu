@@ -76,6 +76,97 @@ pf_status kv_quant_rows(const float* qkv, int ldqkv, int k_col, int v_col, int M
 }
 
 // ---------------------------------------------------------------------------
+// The QKV projection's epilogue for a K-split launch, fused with the staging:
+// per row, sum the int32 slices exactly, v = ((float)acc * a_s[m]) * w_s[n]
+// (matmul_quantized's roundings, src/matmul_neon.cpp:176-180), rotate the q
+// and k columns by adjacent pairs at the row's position (src/engine.cpp:737-748,
+// the same arithmetic as the GEMM's EPI_QKV), write the fp32 row, and quantize
+// each kv head's K and V as kv_quant_kernel does.  One CTA of 8 warps per row;
+// warp w takes the 64-column groups w, w + 8, ..., lane l columns 2l, 2l + 1.
+// ---------------------------------------------------------------------------
+constexpr int kQkvMaxParts = 4;
+constexpr int kQkvGroups = 8;  // 64-column groups per warp (n <= 4096)
+
+__global__ void __launch_bounds__(256) qkv_finish_kernel(const int32_t* __restrict__ parts, int n_parts,
+                                                         int64_t part_stride, const float* __restrict__ a_s,
+                                                         const float* __restrict__ w_s, int N, int M,
+                                                         const float* __restrict__ rope_cos,
+                                                         const float* __restrict__ rope_sin,
+                                                         const int* __restrict__ row_pos, int rope_cols, int hd,
+                                                         float* __restrict__ qkv, int k_col, int v_col, int G,
+                                                         Staged st) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the attention may start streaming the cache
+    const int m = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (m >= M) return;
+    const float as = a_s[m];
+    const int pos = row_pos[m];
+    const int ngroups = N / 64;
+    // every load of the row first
+    int2 acc[kQkvGroups];
+    float2 ws[kQkvGroups], cs[kQkvGroups];
+#pragma unroll
+    for (int k = 0; k < kQkvGroups; k++) {
+        const int grp = warp + 8 * k;
+        const bool in = grp < ngroups;
+        const int c0 = grp * 64 + 2 * lane;
+        acc[k] = make_int2(0, 0);
+#pragma unroll
+        for (int s2 = 0; s2 < kQkvMaxParts; s2++) {
+            const int2 v = (in && s2 < n_parts)
+                               ? __ldcg(reinterpret_cast<const int2*>(parts + s2 * part_stride + (size_t)m * N + c0))
+                               : make_int2(0, 0);
+            acc[k].x += v.x;
+            acc[k].y += v.y;
+        }
+        ws[k] = in ? *reinterpret_cast<const float2*>(w_s + c0) : make_float2(0.f, 0.f);
+        const bool rot = in && c0 < rope_cols;
+        const size_t o = (size_t)pos * (hd >> 1) + ((c0 % hd) >> 1);
+        cs[k] = rot ? make_float2(rope_cos[o], rope_sin[o]) : make_float2(1.f, 0.f);
+    }
+#pragma unroll
+    for (int k = 0; k < kQkvGroups; k++) {
+        const int grp = warp + 8 * k;
+        if (grp >= ngroups) break;  // uniform over the warp
+        const int c0 = grp * 64 + 2 * lane;
+        float v0 = __fmul_rn(__fmul_rn(__int2float_rn(acc[k].x), as), ws[k].x);
+        float v1 = __fmul_rn(__fmul_rn(__int2float_rn(acc[k].y), as), ws[k].y);
+        if (c0 < rope_cols) {
+            const float r0 = __fsub_rn(__fmul_rn(v0, cs[k].x), __fmul_rn(v1, cs[k].y));
+            const float r1 = __fadd_rn(__fmul_rn(v0, cs[k].y), __fmul_rn(v1, cs[k].x));
+            v0 = r0;
+            v1 = r1;
+        }
+        *reinterpret_cast<float2*>(qkv + (size_t)m * N + c0) = make_float2(v0, v1);
+        if (grp * 64 >= k_col) {  // a K or V head: stage it (the group is one head)
+            const bool is_k = grp * 64 < v_col;
+            const int g = (grp * 64 - (is_k ? k_col : v_col)) / 64;
+            int8_t a, b;
+            float sc;
+            quant64_warp(v0, v1, a, b, sc);
+            const size_t wid = (size_t)m * G + g;
+            int8_t* dst = (is_k ? st.k : st.v) + wid * 64 + 2 * lane;
+            dst[0] = a;
+            dst[1] = b;
+            if (lane == 0) (is_k ? st.ks : st.vs)[wid] = sc;
+        }
+    }
+}
+
+pf_status qkv_finish(const int32_t* parts, int n_parts, int64_t part_stride, const float* a_s, const float* w_s,
+                     int N, int M, const float* rope_cos, const float* rope_sin, const int* row_pos, int rope_cols,
+                     int hd, float* qkv, int k_col, int v_col, int G, Staged st, cudaStream_t stream) {
+    PF_CHECK(hd == 64, "qkv_finish: head_dim must be 64");
+    PF_CHECK(n_parts >= 1 && n_parts <= kQkvMaxParts && part_stride >= (int64_t)M * N, "qkv_finish: bad slices");
+    PF_CHECK(N % 64 == 0 && N / 64 <= 8 * kQkvGroups, "qkv_finish: N=%d must be a multiple of 64, at most %d", N,
+             512 * kQkvGroups);
+    PF_CHECK(k_col % 64 == 0 && v_col % 64 == 0 && k_col <= v_col && v_col + G * 64 <= N && rope_cols <= v_col,
+             "qkv_finish: bad column layout");
+    qkv_finish_kernel<<<M, 256, 0, stream>>>(parts, n_parts, part_stride, a_s, w_s, N, M, rope_cos, rope_sin,
+                                             row_pos, rope_cols, hd, qkv, k_col, v_col, G, st);
+    return launch_check("qkv_finish");
+}
+
+// ---------------------------------------------------------------------------
 // Pool entries a batch finalizes between its first and last row
 // (src/kv_cache.cpp:77-109): the committed fp64 accumulator plus the evicted
 // ring entries, added in eviction order, mean = (float)(acc * (1.0f/pb)),

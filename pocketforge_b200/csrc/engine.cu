@@ -108,8 +108,8 @@ struct pf_engine {
     int32_t* gws = nullptr;
     int* gcnt = nullptr;
     size_t gws_elems = 0, gcnt_elems = 0;
-    // int32 partial products of the K-split residual projections (O, down):
-    // [splits][M][d], summed by resid_rmsnorm_quant.
+    // int32 partial products of the K-split projections, [splits][M][N]: O
+    // and down (summed by resid_rmsnorm_quant), QKV (summed by qkv_finish).
     int32_t* rws = nullptr;
     size_t rws_elems = 0;
     // Split-context attention: partial softmax states and arrival counters.
@@ -247,15 +247,22 @@ struct pf_engine {
             sl.vs = stage.vs + (size_t)l * sM * G;
             PF_TRY(norm_rows(&pend, attn_norm + (size_t)l * d, M, nullptr));
             {
+                // K split into int32 slices (the tiles alone fill half the SMs);
+                // qkv_finish applies the scales and RoPE and stages K / V.
                 GemmParams p;
                 p.A = xq; p.lda = d; p.a_scale = xs; p.M = M; p.N = NQKV; p.K = d;
                 p.W = w_qkv[l]; p.wf = fmt_qkv; p.w_scale = s_qkv[l];
-                p.epi = EPI_QKV; p.out = qkv; p.ldo = NQKV;
-                p.rope_cos = rope_cos; p.rope_sin = rope_sin; p.row_pos = rb.row_pos;
-                p.rope_cols = NQ + NK; p.head_dim = hd;
-                PF_TRY(gemm(p, 1));
+                p.epi = EPI_I32; p.out_i32 = rws; p.ldo = NQKV;
+                p.splits = gemm_tc_slices(M, NQKV, d);
+                p.slice_stride = (int64_t)M * NQKV;
+                PF_CHECK((size_t)p.splits * M * NQKV <= rws_elems, "projection workspace too small");
+                p.pdl = true;
+                PF_TRY(tbegin(1));
+                PF_TRY(gemm_tc_launch(p, 1, Mcap, st));
+                PF_TRY(tend());
+                PF_TRY(qkv_finish(rws, p.splits, p.slice_stride, xs, s_qkv[l], NQKV, M, rope_cos, rope_sin, rb.row_pos,
+                                  NQ + NK, hd, qkv, NQ, NQ + NK, G, sl, st));
             }
-            PF_TRY(kv_quant_rows(qkv, NQKV, NQ, NQ + NK, M, nullptr, G, hd, sl, st));
             if (evicting) PF_TRY(kv_pool_spec(kv, l, rb, sp, st));
             PF_TRY(tbegin(0));
             if (attention_decode_supported(kv, H, rb.max_rows)) {
@@ -627,8 +634,10 @@ pf_status pf_engine_create(const pf_model_config* c, int32_t max_seqs, int32_t m
     // split-K is only chosen below 2*148 output tiles of 64x64
     e->gws_elems = (size_t)3 * 296 * 64 * 64;
     E_TRY(dalloc(&e->gws, e->gws_elems, o));
-    for (int m = 1; m <= e->Mcap; m++)  // slices of the K-split residual projections, any row count
-        e->rws_elems = std::max(e->rws_elems, (size_t)std::max(gemm_tc_slices(m, d, e->NQ), gemm_tc_slices(m, d, F)) * m * d);
+    for (int m = 1; m <= e->Mcap; m++)  // slices of the K-split projections, any row count
+        e->rws_elems = std::max({e->rws_elems,
+                                 (size_t)std::max(gemm_tc_slices(m, d, e->NQ), gemm_tc_slices(m, d, F)) * m * d,
+                                 (size_t)gemm_tc_slices(m, e->NQKV, d) * m * e->NQKV});
     E_TRY(dalloc(&e->rws, e->rws_elems, o));
     e->attn_part_floats = attention_decode_work_floats(max_seqs, G, pf_engine::kMaxAttnSplits);
     e->attn_cnt_elems = (size_t)max_seqs * G;

@@ -75,6 +75,12 @@ struct SpecPool {
 pf_status kv_quant_rows(const float* qkv, int ldqkv, int k_col, int v_col, int M, const int* m_dev, int G, int hd,
                         Staged st, cudaStream_t stream);
 pf_status kv_pool_spec(const KvCache& kv, int layer, const RowBatch& rb, SpecPool sp, cudaStream_t stream);
+// The QKV projection from K-split int32 slices ([n_parts][M][N] at part_stride):
+// scales, RoPE on columns [0, rope_cols), the fp32 rows into qkv (row stride
+// N), and the staged K/V of every kv head (as kv_quant_rows).
+pf_status qkv_finish(const int32_t* parts, int n_parts, int64_t part_stride, const float* a_s, const float* w_s,
+                     int N, int M, const float* rope_cos, const float* rope_sin, const int* row_pos, int rope_cols,
+                     int hd, float* qkv, int k_col, int v_col, int G, Staged st, cudaStream_t stream);
 pf_status attention(const KvCache& kv, int layer, const RowBatch& rb, const float* qkv, int ldqkv, int k_col,
                     int v_col, int H, Staged st, SpecPool sp, float* out, int ldo, cudaStream_t stream);
 // Tensor-core variant for batches of at most 32 / (H/G) rows per sequence
