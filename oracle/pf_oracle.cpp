@@ -726,11 +726,16 @@ struct SkipState {
         if (layer < 2 || layer >= L - 2) t = -1.0f;
         return t;
     }
-    bool should_skip(uint32_t layer, const float* x, int order) {
+    // margin (optional): |delta - threshold| / threshold of this decision, a
+    // test diagnostic (a decision within float rounding of its threshold can
+    // go either way in another summation order).
+    bool should_skip(uint32_t layer, const float* x, int order, float* margin = nullptr) {
         if (layer >= L) return false;
         float* c = cache.data() + (size_t)layer * d;
         const float dl = delta(x, c, d, order);
-        const bool skip = dl < layer_threshold(layer);
+        const float lt = layer_threshold(layer);
+        if (margin) *margin = lt > 0.0f ? std::fabs(dl - lt) / lt : INFINITY;
+        const bool skip = dl < lt;
         if (!skip) std::memcpy(c, x, d * sizeof(float));
         return skip;
     }
@@ -770,6 +775,7 @@ struct Engine {
     std::vector<Seq> seqs;
     std::vector<float> last_logits;  // [n_seqs*(K+1)][V]
     int64_t ffn_computed = 0, ffn_skipped = 0;
+    float skip_margin = INFINITY;  // smallest decision margin seen (test diagnostic)
 
     uint32_t d() const { return (uint32_t)cfg.n_embd; }
     uint32_t K() const { return (uint32_t)cfg.n_mtp_heads; }
@@ -867,7 +873,9 @@ struct Engine {
             mm_quant(att.data(), w[PF_MAT_O][l].data(), o.data(), 1, D, H * hd, rs[PF_MAT_O][l].data(), nullptr);
             for (uint32_t i = 0; i < D; i++) x[i] += o[i];
             rmsnorm(nrm.data(), x.data(), ffn_norm.data() + (size_t)l * D, D, cfg.norm_eps, order);
-            const bool skip = cfg.skip_enabled ? s.skip.should_skip(l, nrm.data(), order) : false;
+            float mg = INFINITY;
+            const bool skip = cfg.skip_enabled ? s.skip.should_skip(l, nrm.data(), order, &mg) : false;
+            skip_margin = std::min(skip_margin, mg);
             if (skip) {
                 ffn_skipped++;
                 continue;
@@ -1186,6 +1194,7 @@ void po_engine_read_mtp_logits(void* ep, float* out) {
     for (size_t b = 0; b < e->seqs.size(); b++)
         std::memcpy(out + b * n, e->seqs[b].mtp_logits.data(), n * sizeof(float));
 }
+float po_engine_skip_margin(void* ep) { return ((po::Engine*)ep)->skip_margin; }
 void po_engine_read_skip_counts(void* ep, int64_t* comp, int64_t* skip) {
     auto* e = (po::Engine*)ep;
     *comp = e->ffn_computed;

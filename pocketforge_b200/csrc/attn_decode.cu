@@ -64,6 +64,7 @@ constexpr int NW = 4;    // warps per CTA
 constexpr int NSW = 3;   // cp.async stages per warp
 constexpr int BIG = 1 << 30;
 constexpr int PART = 68; // floats per (split, row) partial state: m, l, pad, pad, o[64]
+constexpr int NEXMAX = 4; // extra blocks (sinks, in-batch pool entries, earlier rows of the batch)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kMaxLead = 8.0f;  // log2 units a block max may exceed the reference before it moves
 
@@ -177,14 +178,14 @@ struct __align__(16) BlockBuf {
     float ks[32], vs[32];
 };
 
-template <int MT>
+template <int MT, int NEX>
 struct __align__(16) AttnSmem {
     uint4 qf[MT][3][2][32];  // query digit planes as A fragments [m-tile][plane][k-step][lane]
     float fr[QR];            // per row: f = s * log2(e) / 8 (0 for padding rows)
     float s_self[QR];        // self-term score, raw units
     float v_self[QR][64];    // self-term values
-    BlockBuf ex;             // the extra block
-    int ex_lo[32], ex_hi[32];// rows of the sequence that see each extra entry
+    BlockBuf ex[NEX];        // the extra blocks
+    int ex_lo[32 * NEX], ex_hi[32 * NEX];  // rows of the sequence that see each extra entry
     union {
         BlockBuf ring[NW][NSW];
         struct {
@@ -198,18 +199,23 @@ struct __align__(16) AttnSmem {
 
 }  // namespace
 
-template <int MT>
+template <int MT, int NEX>
 __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int layer, RowBatch rb, const float* __restrict__ qkv,
                                                           int ld, int k_col, int v_col, int H, Staged st, SpecPool sp,
-                                                          AttnWork aw, float* __restrict__ out, int ldo, uint32_t* err) {
+                                                          AttnWork aw, int nsplit, float* __restrict__ out, int ldo,
+                                                          uint32_t* err) {
     extern __shared__ __align__(16) uint8_t attn_smem_raw[];
-    AttnSmem<MT>& sm = *reinterpret_cast<AttnSmem<MT>*>(attn_smem_raw);
-    const int b = blockIdx.x, g = blockIdx.y, split = blockIdx.z, nsplit = gridDim.z;
+    AttnSmem<MT, NEX>& sm = *reinterpret_cast<AttnSmem<MT, NEX>*>(attn_smem_raw);
+    const int b = blockIdx.x, g = blockIdx.y;
+    const int split = (int)blockIdx.z % nsplit, rg = (int)blockIdx.z / nsplit;
     const int n = rb.n[b];
-    if (n == 0) return;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
     const int qpk = H / kv.G;
-    const int rows = qpk * n;  // <= 16 * MT (checked on the host)
+    const int rpc = QR / qpk;      // sequence rows per CTA
+    const int r0 = rg * rpc;       // this CTA's sequence rows [r0, r0 + nr)
+    if (r0 >= n) return;
+    const int nr = min(rpc, n - r0);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
+    const int rows = qpk * nr;  // <= 16 * MT (checked on the host)
     const int L0 = rb.len0[b], row0 = rb.row0[b];
     const int plast = L0 + n - 1;
     const int cs = min(L0, kv.S);
@@ -220,15 +226,18 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
     const int s0 = (qlo - kv.S) % kv.Wr;  // ring slot of the oldest window position
     const size_t u = kv.unit(b, layer, g);
     const int n_spec = npool - nb0;
-    const int n_ex = cs + n_spec + (n - 1);
-    if (n_ex > 32 || rows > 16 * MT) {  // excluded by the host; never index past the tiles
+    // earlier rows of the batch: row r sees staged rows j < r, and this CTA's
+    // last row is r0 + nr - 1
+    const int n_ex = cs + n_spec + (r0 + nr - 1);
+    if (n_ex > 32 * NEX || rows > 16 * MT) {  // excluded by the host; never index past the tiles
         if (tid == 0 && err) atomicOr(err, ERR_BOUNDS);
         return;
     }
     const int pool_blocks = (nb0 + 31) / 32;
     const int ring_blocks = (nwin + 31) / 32;
     const int nkv = pool_blocks + ring_blocks;  // blocks that stream from memory
-    const int nblk = nkv + (n_ex > 0 ? 1 : 0);
+    const int nex = (n_ex + 31) / 32;
+    const int nblk = nkv + nex;
     const int b_begin = (int)((int64_t)nblk * split / nsplit);
     const int b_end = (int)((int64_t)nblk * (split + 1) / nsplit);
 
@@ -291,20 +300,29 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
             lo = j + 1;
         }
     };
-    const bool own_ex = nkv >= b_begin && nkv < b_end;  // this split owns the extra block
-    const int ex_e = tid >> 2, ex_q4 = tid & 3;          // entry, dims [16*q4, 16*q4 + 16)
-    uint4 ex_k = make_uint4(0, 0, 0, 0), ex_v = make_uint4(0, 0, 0, 0);
-    float ex_ks = 0.0f, ex_vs = 0.0f;
-    int ex_lo = BIG, ex_hi = -1;
-    if (own_ex && ex_e < n_ex) {
-        const int8_t *kp, *vp;
-        const float *ksp, *vsp;
-        ex_src(ex_e, kp, vp, ksp, vsp, ex_lo);
-        ex_hi = BIG;
-        ex_k = *reinterpret_cast<const uint4*>(kp + 16 * ex_q4);
-        ex_v = *reinterpret_cast<const uint4*>(vp + 16 * ex_q4);
-        ex_ks = *ksp;
-        ex_vs = *vsp;
+    // this split owns some extra block: it assembles all of them
+    const bool own_ex = nex > 0 && b_end > nkv && b_begin < nblk;
+    // task t (< nex * 128): entry t >> 2, dims [16*(t&3), +16)
+    uint4 ex_k[NEX], ex_v[NEX];
+    float ex_ks[NEX], ex_vs[NEX];
+    int ex_lo[NEX];
+#pragma unroll
+    for (int x = 0; x < NEX; x++) {
+        const int e = (tid + 128 * x) >> 2, q4 = tid & 3;
+        ex_k[x] = make_uint4(0, 0, 0, 0);
+        ex_v[x] = make_uint4(0, 0, 0, 0);
+        ex_ks[x] = 0.0f;
+        ex_vs[x] = 0.0f;
+        ex_lo[x] = BIG;
+        if (own_ex && e < n_ex) {
+            const int8_t *kp, *vp;
+            const float *ksp, *vsp;
+            ex_src(e, kp, vp, ksp, vsp, ex_lo[x]);
+            ex_k[x] = *reinterpret_cast<const uint4*>(kp + 16 * q4);
+            ex_v[x] = *reinterpret_cast<const uint4*>(vp + 16 * q4);
+            ex_ks[x] = *ksp;
+            ex_vs[x] = *vsp;
+        }
     }
 
     // ---- queries -> fp16 fragment planes; self-term score and value ----
@@ -314,7 +332,7 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
     for (int k = 0; k < RPW; k++) {
         const int ri = warp + NW * k;
         const bool in = ri < rows;
-        const int hh = in ? ri / n : 0, r = in ? ri % n : 0;
+        const int hh = in ? ri / nr : 0, r = in ? r0 + ri % nr : 0;
         const float* row = qkv + (size_t)(row0 + r) * ld;
         const float* q = row + (size_t)(g + hh * kv.G) * 64;
         qx[k][0] = in ? q[lane] : 0.0f;
@@ -362,16 +380,23 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
     }
 
     if (own_ex) {
-        *reinterpret_cast<uint4*>(&sm.ex.k[ex_e][16 * ex_q4]) = ex_k;
-        const uint8_t* vb = reinterpret_cast<const uint8_t*>(&ex_v);
-        const int pos = kv_vpos(ex_e);
 #pragma unroll
-        for (int i = 0; i < 16; i++) sm.ex.v[(16 * ex_q4 + i) * 32 + pos] = (int8_t)vb[i];
-        if (ex_q4 == 0) {
-            sm.ex.ks[ex_e] = ex_ks;
-            sm.ex.vs[ex_e] = ex_vs;
-            sm.ex_lo[ex_e] = ex_lo;
-            sm.ex_hi[ex_e] = ex_hi;
+        for (int x = 0; x < NEX; x++) {
+            const int e = (tid + 128 * x) >> 2, q4 = tid & 3;
+            if (e >= 32 * nex) break;
+            BlockBuf& xb = sm.ex[e >> 5];
+            const int el = e & 31;
+            *reinterpret_cast<uint4*>(&xb.k[el][16 * q4]) = ex_k[x];
+            const uint8_t* vb = reinterpret_cast<const uint8_t*>(&ex_v[x]);
+            const int pos = kv_vpos(el);
+#pragma unroll
+            for (int i = 0; i < 16; i++) xb.v[(16 * q4 + i) * 32 + pos] = (int8_t)vb[i];
+            if (q4 == 0) {
+                xb.ks[el] = ex_ks[x];
+                xb.vs[el] = ex_vs[x];
+                sm.ex_lo[e] = ex_lo[x];
+                sm.ex_hi[e] = e < n_ex ? BIG : -1;
+            }
         }
     }
     __syncthreads();
@@ -385,7 +410,7 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
         for (int h = 0; h < 2; h++) {
             const int ri = mt * 16 + gid + 8 * h;
             fr[mt][h] = sm.fr[ri];
-            rr[mt][h] = ri < rows ? ri % n : -1;  // padding row: every entry has lo >= 0
+            rr[mt][h] = ri < rows ? r0 + ri % nr : -1;  // padding row: every entry has lo >= 0
             mref[mt][h] = -INFINITY;
             lsum[mt][h] = 0.0f;
         }
@@ -407,15 +432,15 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
         __syncwarp();  // every lane's copies of block i landed; slot (i - 1) % NSW is free
         load_block(i + NSW - 1, slot == 0 ? NSW - 1 : slot - 1);
         cp_commit();
-        const bool is_ex = blk == nkv;
-        const BlockBuf& bb = is_ex ? sm.ex : sm.u.ring[warp][slot];
+        const bool is_ex = blk >= nkv;
+        const BlockBuf& bb = is_ex ? sm.ex[blk - nkv] : sm.u.ring[warp][slot];
         slot = (slot + 1 == NSW) ? 0 : slot + 1;
 
         // ---- visibility of entry `lane`: query rows [lo, hi] of the sequence ----
         int lo = BIG, hi = -1;
         if (is_ex) {
-            lo = sm.ex_lo[lane];
-            hi = sm.ex_hi[lane];
+            lo = sm.ex_lo[(blk - nkv) * 32 + lane];
+            hi = sm.ex_hi[(blk - nkv) * 32 + lane];
         } else if (blk < pool_blocks) {
             if (blk * 32 + lane < nb0) lo = 0, hi = BIG;
         } else {
@@ -426,7 +451,7 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
             }
         }
         const bool valid = hi >= 0 && lo < BIG;
-        const bool full = __all_sync(0xffffffffu, valid && lo <= 0 && hi >= n - 1);
+        const bool full = __all_sync(0xffffffffu, valid && lo <= r0 && hi >= r0 + nr - 1);  // every row of this CTA
 
         // ---- v-scale reference: a power of two per warp, raised when a block's
         // scales outgrow it (the accumulators are rescaled exactly) ----
@@ -646,7 +671,7 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
     }
 
     // ---- more than one split: publish, and let the last split merge ----
-    const size_t item = (size_t)b * kv.G + g;
+    const size_t item = ((size_t)b * kv.G + g) * (gridDim.z / nsplit) + rg;  // (sequence, kv head, row group)
     if (nsplit > 1) {
         float* part = aw.part + (item * nsplit + split) * QR * PART;
         for (int ri = warp; ri < rows; ri += NW) {
@@ -673,7 +698,7 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
     // ---- final: all splits' states + the self term -> output rows ----
     __syncwarp();  // (one split) this warp's rows of cm / cl / acc[0] are written
     for (int ri = warp; ri < rows; ri += NW) {
-        const int hh = ri / n, r = ri % n;
+        const int hh = ri / nr, r = r0 + ri % nr;
         const int h = g + hh * kv.G;
         const float ss = sm.s_self[ri], fq = sm.fr[ri];
         float m = ss, l, o0, o1;
@@ -709,9 +734,14 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
 }
 
 bool attention_decode_supported(const KvCache& kv, int H, int max_rows) {
-    const int rows = (H / kv.G) * max_rows;
     const int spec = max_rows > 1 ? ceil_div(max_rows - 1, kv.pb) + 1 : 1;  // pool entries a batch can finalize
-    return rows <= QR && kv.S + spec + max_rows - 1 <= 32;
+    return H / kv.G <= QR && kv.S + spec + max_rows - 1 <= 32 * NEXMAX;
+}
+
+// Sequence rows per CTA and row groups per (sequence, kv head).
+static int attn_rows_per_cta(const KvCache& kv, int H) { return QR / (H / kv.G); }
+int attention_decode_row_groups(const KvCache& kv, int H, int max_rows) {
+    return ceil_div(std::max(1, max_rows), attn_rows_per_cta(kv, H));
 }
 
 int attention_decode_splits(int nb, int G, int max_splits) {
@@ -721,20 +751,22 @@ int attention_decode_splits(int nb, int G, int max_splits) {
     return std::max(1, std::min(max_splits, (2 * 148) / items));
 }
 
-size_t attention_decode_work_floats(int nb, int G, int nsplit) { return (size_t)nb * G * nsplit * QR * PART; }
+size_t attention_decode_work_floats(int nb, int G, int nsplit, int nrg) {
+    return (size_t)nb * G * nrg * nsplit * QR * PART;
+}
 
-template <int MT>
+template <int MT, int NEX>
 static pf_status launch_decode(const KvCache& kv, int layer, const RowBatch& rb, const float* qkv, int ldqkv, int k_col,
                                int v_col, int H, Staged st, SpecPool sp, const AttnWork& aw, float* out, int ldo,
                                cudaStream_t stream) {
-    const int smem = (int)sizeof(AttnSmem<MT>);
+    const int smem = (int)sizeof(AttnSmem<MT, NEX>);
     static bool attr = false;
     if (!attr) {
-        PF_CUDA(cudaFuncSetAttribute(attn_decode_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        PF_CUDA(cudaFuncSetAttribute(attn_decode_kernel<MT, NEX>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         attr = true;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(rb.nb, kv.G, aw.nsplit);
+    cfg.gridDim = dim3(rb.nb, kv.G, aw.nsplit * attention_decode_row_groups(kv, H, rb.max_rows));
     cfg.blockDim = dim3(128);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
@@ -743,8 +775,8 @@ static pf_status launch_decode(const KvCache& kv, int layer, const RowBatch& rb,
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    PF_CUDA(cudaLaunchKernelEx(&cfg, attn_decode_kernel<MT>, kv, layer, rb, qkv, ldqkv, k_col, v_col, H, st, sp, aw, out,
-                               ldo, device_error_flag()));
+    PF_CUDA(cudaLaunchKernelEx(&cfg, attn_decode_kernel<MT, NEX>, kv, layer, rb, qkv, ldqkv, k_col, v_col, H, st, sp, aw,
+                               aw.nsplit, out, ldo, device_error_flag()));
     return launch_check("attention_decode");
 }
 
@@ -753,13 +785,21 @@ pf_status attention_decode(const KvCache& kv, int layer, const RowBatch& rb, con
                            cudaStream_t stream) {
     PF_CHECK(kv.hd == 64, "attention_decode: head_dim must be 64");
     PF_CHECK(attention_decode_supported(kv, H, rb.max_rows), "attention_decode: too many query rows");
-    PF_CHECK(aw.nsplit >= 1 && aw.nsplit <= 65535, "attention_decode: bad split count");
-    PF_CHECK(aw.nsplit == 1 || (aw.part && aw.cnt && aw.part_floats >= attention_decode_work_floats(rb.nb, kv.G, aw.nsplit) &&
-                                aw.cnt_elems >= (size_t)rb.nb * kv.G),
+    const int nrg = attention_decode_row_groups(kv, H, rb.max_rows);
+    PF_CHECK(aw.nsplit >= 1 && aw.nsplit * nrg <= 65535, "attention_decode: bad split count");
+    PF_CHECK(aw.nsplit == 1 ||
+                 (aw.part && aw.cnt && aw.part_floats >= attention_decode_work_floats(rb.nb, kv.G, aw.nsplit, nrg) &&
+                  aw.cnt_elems >= (size_t)rb.nb * kv.G * nrg),
              "attention_decode: workspace too small for %d splits", aw.nsplit);
-    if ((H / kv.G) * rb.max_rows <= 16)
-        return launch_decode<1>(kv, layer, rb, qkv, ldqkv, k_col, v_col, H, st, sp, aw, out, ldo, stream);
-    return launch_decode<2>(kv, layer, rb, qkv, ldqkv, k_col, v_col, H, st, sp, aw, out, ldo, stream);
+    // one extra block for verify batches, up to NEXMAX for prefill chunks
+    const int spec = rb.max_rows > 1 ? ceil_div(rb.max_rows - 1, kv.pb) + 1 : 1;
+    const bool one_ex = kv.S + spec + rb.max_rows - 1 <= 32;
+    const bool mt1 = (H / kv.G) * std::min(rb.max_rows, attn_rows_per_cta(kv, H)) <= 16;
+    if (one_ex)
+        return mt1 ? launch_decode<1, 1>(kv, layer, rb, qkv, ldqkv, k_col, v_col, H, st, sp, aw, out, ldo, stream)
+                   : launch_decode<2, 1>(kv, layer, rb, qkv, ldqkv, k_col, v_col, H, st, sp, aw, out, ldo, stream);
+    return mt1 ? launch_decode<1, NEXMAX>(kv, layer, rb, qkv, ldqkv, k_col, v_col, H, st, sp, aw, out, ldo, stream)
+               : launch_decode<2, NEXMAX>(kv, layer, rb, qkv, ldqkv, k_col, v_col, H, st, sp, aw, out, ldo, stream);
 }
 
 }  // namespace pf

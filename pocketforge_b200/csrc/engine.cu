@@ -267,7 +267,12 @@ struct pf_engine {
             PF_TRY(tbegin(0));
             if (attention_decode_supported(kv, H, rb.max_rows)) {
                 AttnWork aw;
-                aw.nsplit = attn_splits > 0 ? attn_splits : attention_decode_splits(rb.nb, G, kMaxAttnSplits);
+                const int nrg = attention_decode_row_groups(kv, H, rb.max_rows);
+                aw.nsplit = attn_splits > 0 ? attn_splits : attention_decode_splits(rb.nb * nrg, G, kMaxAttnSplits);
+                // (wide prefill batches have row groups enough: no split there)
+                if (attention_decode_work_floats(rb.nb, G, aw.nsplit, nrg) > attn_part_floats ||
+                    (size_t)rb.nb * G * nrg > attn_cnt_elems)
+                    aw.nsplit = 1;
                 aw.part = attn_part;
                 aw.part_floats = attn_part_floats;
                 aw.cnt = attn_cnt;
@@ -639,8 +644,8 @@ pf_status pf_engine_create(const pf_model_config* c, int32_t max_seqs, int32_t m
                                  (size_t)std::max(gemm_tc_slices(m, d, e->NQ), gemm_tc_slices(m, d, F)) * m * d,
                                  (size_t)gemm_tc_slices(m, e->NQKV, d) * m * e->NQKV});
     E_TRY(dalloc(&e->rws, e->rws_elems, o));
-    e->attn_part_floats = attention_decode_work_floats(max_seqs, G, pf_engine::kMaxAttnSplits);
-    e->attn_cnt_elems = (size_t)max_seqs * G;
+    e->attn_part_floats = attention_decode_work_floats(max_seqs, G, pf_engine::kMaxAttnSplits, 1);
+    e->attn_cnt_elems = (size_t)max_seqs * G * pf_engine::kMaxAttnSplits;
     E_TRY(dalloc(&e->attn_part, e->attn_part_floats, o));
     E_TRY(dalloc(&e->attn_cnt, e->attn_cnt_elems, o));
     if (cudaMemset(e->attn_cnt, 0, e->attn_cnt_elems * sizeof(int)) != cudaSuccess) return fail(PF_ERR_CUDA);
@@ -880,7 +885,9 @@ pf_status pf_engine_prefill(pf_engine* e, int32_t n, const int32_t* tokens, cons
     PF_CUDA(cudaMemsetAsync(e->sb.seq_len, 0, e->max_seqs * 4, st));
 
     // Chunked prefill: every chunk is a row batch through all layers, committed whole.
-    const int C = std::max(1, std::min(e->kv.Wr, e->Mcap / n));
+    // (at most as many rows per sequence as the tensor-core attention takes)
+    int C = std::max(1, std::min(e->kv.Wr, e->Mcap / n));
+    while (C > 1 && !attention_decode_supported(e->kv, e->H, C)) C--;
     std::vector<int> row_tok, row_pos, row0(n), cnt(n), len0(n), last_idx(n, -1);
     std::vector<float> dummy;
     for (int c0 = 0; c0 < maxlen; c0 += C) {

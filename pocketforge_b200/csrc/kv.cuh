@@ -83,11 +83,12 @@ pf_status qkv_finish(const int32_t* parts, int n_parts, int64_t part_stride, con
                      int hd, float* qkv, int k_col, int v_col, int G, Staged st, cudaStream_t stream);
 pf_status attention(const KvCache& kv, int layer, const RowBatch& rb, const float* qkv, int ldqkv, int k_col,
                     int v_col, int H, Staged st, SpecPool sp, float* out, int ldo, cudaStream_t stream);
-// Tensor-core variant for batches of at most 32 / (H/G) rows per sequence
-// whose sink, in-batch pool entries and earlier rows fit one 32-entry block.
-// The context of each (sequence, kv head) is split over `nsplit` CTAs whose
-// partial softmax states meet in `part`; `cnt` ([nb][G] ints, zero before the
-// first launch) counts the arrivals and is left zero.
+// Tensor-core variant: one CTA per (sequence, kv head, group of 32 / (H/G)
+// rows of the sequence), for batches whose sink, in-batch pool entries and
+// earlier rows fit four 32-entry blocks.  The context of each (sequence, kv
+// head, row group) is split over `nsplit` CTAs whose partial softmax states
+// meet in `part`; `cnt` ([nb][G][row groups] ints, zero before the first
+// launch) counts the arrivals and is left zero.
 struct AttnWork {
     int nsplit = 1;
     float* part = nullptr;
@@ -97,7 +98,8 @@ struct AttnWork {
 };
 bool attention_decode_supported(const KvCache& kv, int H, int max_rows);
 int attention_decode_splits(int nb, int G, int max_splits);
-size_t attention_decode_work_floats(int nb, int G, int nsplit);
+int attention_decode_row_groups(const KvCache& kv, int H, int max_rows);
+size_t attention_decode_work_floats(int nb, int G, int nsplit, int nrg);
 pf_status attention_decode(const KvCache& kv, int layer, const RowBatch& rb, const float* qkv, int ldqkv, int k_col,
                            int v_col, int H, Staged st, SpecPool sp, const AttnWork& aw, float* out, int ldo,
                            cudaStream_t stream);

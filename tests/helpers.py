@@ -156,6 +156,10 @@ class OracleEngine:
         self.L.po_engine_read_mtp_logits(self.h, a)
         return a.reshape(self.n, self.cfg.n_mtp_heads, -1)
 
+    def skip_margin(self) -> float:
+        """Smallest |delta - threshold| / threshold of any layer-skip decision so far."""
+        return float(self.L.po_engine_skip_margin(self.h))
+
     def skip_counts(self):
         a, b = C.c_int64(), C.c_int64()
         self.L.po_engine_read_skip_counts(self.h, C.byref(a), C.byref(b))
