@@ -212,7 +212,12 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
     const int qpk = H / kv.G;
     const int rpc = QR / qpk;      // sequence rows per CTA
     const int r0 = rg * rpc;       // this CTA's sequence rows [r0, r0 + nr)
-    if (r0 >= n) return;
+    if (r0 >= n) {
+        // (every CTA waits for the previous kernel, so that this grid's
+        // completion implies that kernel's, for the kernels launched after it)
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        return;
+    }
     const int nr = min(rpc, n - r0);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
     const int rows = qpk * nr;  // <= 16 * MT (checked on the host)
@@ -231,6 +236,7 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
     const int n_ex = cs + n_spec + (r0 + nr - 1);
     if (n_ex > 32 * NEX || rows > 16 * MT) {  // excluded by the host; never index past the tiles
         if (tid == 0 && err) atomicOr(err, ERR_BOUNDS);
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         return;
     }
     const int pool_blocks = (nb0 + 31) / 32;
