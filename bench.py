@@ -260,7 +260,9 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
+        torch.cuda.nvtx.range_push("prefill")  # (a range for profilers; free otherwise)
         eng.prefill(host_prompts, seeds)
+        torch.cuda.nvtx.range_pop()
         got = seqs  # the first token comes out of prefill
         for _ in range(args.steps):
             n, em = eng.step()
