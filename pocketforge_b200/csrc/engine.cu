@@ -314,28 +314,52 @@ struct pf_engine {
         return gemm(p, 3);
     }
 
+    // One MTP projection over the digit planes of n rows stacked along M
+    // ([3][n][d]): K split into int32 slices in rws; returns the split count.
+    pf_status mtp_gemm(const void* W, int N, int n, int* parts) {
+        GemmParams p;
+        p.A = digits; p.lda = d; p.M = 3 * n; p.N = N; p.K = d;
+        p.W = W; p.wf = WF_Q4;
+        p.epi = EPI_I32; p.out_i32 = rws; p.ldo = N;
+        p.splits = gemm_tc_slices(3 * n, N, d);
+        p.slice_stride = (int64_t)3 * n * N;
+        PF_CHECK((size_t)p.splits * 3 * n * N <= rws_elems, "projection workspace too small");
+        p.pdl = true;
+        PF_TRY(tbegin(1));
+        PF_TRY(gemm_tc_launch(p, 1, 3 * n, st));
+        PF_TRY(tend());
+        *parts = p.splits;
+        return PF_OK;
+    }
+
     // MTP heads on mtp_cur (n rows): drafts[b][h] (MTPHeads::forward, src/mtp.cpp:47-129).
+    // The digit planes of the rows feed each projection as 3 n stacked rows;
+    // each finishing kernel applies the projection's epilogue and splits its
+    // result for the next one (the head's residual output also feeds the
+    // unembedding and the next head).
     pf_status mtp_chain(int n) {
-        const int64_t plane = (int64_t)Mcap * d;
+        const int64_t plane = (int64_t)n * d;
+        PF_TRY(split_digits(mtp_cur, d, d, n, nullptr, digits, plane, d, dscale, st));
         for (int h = 0; h < K; h++) {
-            PF_TRY(split_digits(mtp_cur, d, d, n, nullptr, digits, plane, d, dscale, st));
-            {
-                GemmParams p;
-                p.A = digits; p.plane_stride = plane; p.lda = d; p.a_scale = dscale; p.M = n; p.N = 2 * d; p.K = d;
-                p.W = mtp_gu[h]; p.wf = WF_Q4; p.w_scale = mtp_gu_s[h];
-                p.epi = EPI_MTP_SWIGLU3; p.out = mtp_act; p.ldo = d;
-                PF_TRY(gemm(p, 3));
-            }
-            PF_TRY(split_digits(mtp_act, d, d, n, nullptr, digits, plane, d, dscale, st));
-            {
-                GemmParams p;
-                p.A = digits; p.plane_stride = plane; p.lda = d; p.a_scale = dscale; p.M = n; p.N = d; p.K = d;
-                p.W = mtp_down[h]; p.wf = WF_Q4; p.w_scale = mtp_down_s[h];
-                p.epi = EPI_MTP_RESID3; p.resid = mtp_cur; p.ldo = d;
-                PF_TRY(gemm(p, 3));
-            }
+            int parts = 0;
+            PF_TRY(mtp_gemm(mtp_gu[h], 2 * d, n, &parts));
+            PF_TRY(mtp_finish(true, rws, parts, (int64_t)3 * n * 2 * d, dscale, mtp_gu_s[h], d, n, nullptr, digits,
+                              dscale, st));
+            PF_TRY(mtp_gemm(mtp_down[h], d, n, &parts));
+            PF_TRY(mtp_finish(false, rws, parts, (int64_t)3 * n * d, dscale, mtp_down_s[h], d, n, mtp_cur, digits,
+                              dscale, st));
             float* lg = mtp_logits + (size_t)h * max_seqs * V;
-            PF_TRY(unembed(mtp_cur, n, lg));
+            {
+                GemmParams p;
+                p.A = digits; p.plane_stride = plane; p.lda = d; p.a_scale = dscale; p.M = n; p.N = V; p.K = d;
+                p.W = emb_packed; p.wf = fmt_emb; p.w_scale_all = emb_gscale;
+                p.epi = EPI_LOGITS3; p.out = lg; p.ldo = V;
+                p.splits = 1;
+                p.pdl = true;
+                PF_TRY(tbegin(1));
+                PF_TRY(gemm_tc_launch(p, 3, n, st));
+                PF_TRY(tend());
+            }
             if (greedy()) {
                 PF_TRY(argmax_rows(lg, V, V, n, nullptr, mtp_tok, st));
             } else {
@@ -643,6 +667,9 @@ pf_status pf_engine_create(const pf_model_config* c, int32_t max_seqs, int32_t m
         e->rws_elems = std::max({e->rws_elems,
                                  (size_t)std::max(gemm_tc_slices(m, d, e->NQ), gemm_tc_slices(m, d, F)) * m * d,
                                  (size_t)gemm_tc_slices(m, e->NQKV, d) * m * e->NQKV});
+    for (int n = 1; n <= max_seqs; n++)  // the MTP heads' projections over 3 n stacked digit rows
+        e->rws_elems = std::max({e->rws_elems, (size_t)gemm_tc_slices(3 * n, 2 * d, d) * 3 * n * 2 * d,
+                                 (size_t)gemm_tc_slices(3 * n, d, d) * 3 * n * d});
     E_TRY(dalloc(&e->rws, e->rws_elems, o));
     e->attn_part_floats = attention_decode_work_floats(max_seqs, G, pf_engine::kMaxAttnSplits, 1);
     e->attn_cnt_elems = (size_t)max_seqs * G * pf_engine::kMaxAttnSplits;

@@ -507,7 +507,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             // Pass 1: per-column values of this thread's row -> its warp's
             // staging rows (row stride HALF + 4 words: conflict-free).
             float* stg = reinterpret_cast<float*>(smem) + (warp - 2) * 32 * Ly::SROW;
-            const float a_s = in_m ? p.a_scale[m] : 0.0f;
+            const float a_s = (in_m && EPI != EPI_I32) ? p.a_scale[m] : 0.0f;  // (int32 slices: no scales)
             const float s_all = __fmul_rn(a_s, p.w_scale_all);
             for (int j = 0; j < HALF / 16; j++) {
                 uint32_t r[P][16];

@@ -293,6 +293,123 @@ pf_status split_digits(const float* x, int n, int ldx, int M, const int* m_dev, 
 }
 
 // ---------------------------------------------------------------------------
+// An MTP head's projection from K-split int32 slices of the digit-plane rows
+// stacked along M ([parts][3 M][N]: rows m, M + m, 2 M + m are the planes of
+// row m), with the GEMM epilogue's arithmetic (comb3 of the exact plane sums,
+// * a_scale[m] * w_scale[col]), then the three digit planes of the result row
+// (as split_digits) for the next projection:
+//   SWIGLU: N = 2 d interleaved (gate, up) columns -> act = mtp_swiglu(g, u)
+//   RESID : N = d, x[m] += value (the residual of the head, updated in place)
+// a_s and qs may be the same array (each row reads its scale first).
+// ---------------------------------------------------------------------------
+constexpr int kMtpMaxParts = 4;
+
+template <bool SWIGLU>
+__global__ void __launch_bounds__(RT) mtp_finish_kernel(const int32_t* __restrict__ parts, int n_parts,
+                                                        int64_t part_stride, const float* a_s,
+                                                        const float* __restrict__ w_s, int d, int M,
+                                                        float* __restrict__ x, int8_t* __restrict__ q, float* qs) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // lets the next GEMM start its prologue
+    __shared__ float sh[33];
+    const int row = blockIdx.x, t = threadIdx.x;
+    if (row >= M) return;
+    constexpr int E = 8;  // d <= 2048
+    const int N = SWIGLU ? 2 * d : d;
+    const float as = a_s[row];
+    // every load first: the three planes' slices of this thread's columns
+    int32_t acc[E][3][SWIGLU ? 2 : 1];
+    float ws[E][SWIGLU ? 2 : 1], xr[E];
+#pragma unroll
+    for (int i = 0; i < E; i++) {
+        const int c = t + i * RT;
+        const bool in = c < d;
+        xr[i] = (!SWIGLU && in) ? x[(size_t)row * d + c] : 0.0f;
+#pragma unroll
+        for (int p = 0; p < 3; p++) {
+            const size_t base = ((size_t)p * M + row) * N;
+            if constexpr (SWIGLU) {
+                acc[i][p][0] = acc[i][p][1] = 0;
+#pragma unroll
+                for (int s2 = 0; s2 < kMtpMaxParts; s2++) {
+                    const int2 v = (in && s2 < n_parts)
+                                       ? __ldcg(reinterpret_cast<const int2*>(parts + s2 * part_stride + base + 2 * c))
+                                       : make_int2(0, 0);
+                    acc[i][p][0] += v.x;
+                    acc[i][p][1] += v.y;
+                }
+            } else {
+                acc[i][p][0] = 0;
+#pragma unroll
+                for (int s2 = 0; s2 < kMtpMaxParts; s2++)
+                    acc[i][p][0] += (in && s2 < n_parts) ? __ldcg(parts + s2 * part_stride + base + c) : 0;
+            }
+        }
+        if constexpr (SWIGLU) {
+            const float2 w2 = in ? *reinterpret_cast<const float2*>(w_s + 2 * c) : make_float2(0.f, 0.f);
+            ws[i][0] = w2.x;
+            ws[i][1] = w2.y;
+        } else {
+            ws[i][0] = in ? w_s[c] : 0.0f;
+        }
+    }
+    const float r = 1.0f / 254.0f;
+    auto comb3 = [&](int32_t a0, int32_t a1, int32_t a2) {
+        return __fadd_rn(__int2float_rn(a0), __fmul_rn(__fadd_rn(__int2float_rn(a1), __fmul_rn(__int2float_rn(a2), r)), r));
+    };
+    float v[E];
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < E; i++) {
+        const int c = t + i * RT;
+        v[i] = 0.0f;
+        if (c >= d) continue;
+        if constexpr (SWIGLU) {
+            const float g = __fmul_rn(__fmul_rn(comb3(acc[i][0][0], acc[i][1][0], acc[i][2][0]), as), ws[i][0]);
+            const float u = __fmul_rn(__fmul_rn(comb3(acc[i][0][1], acc[i][1][1], acc[i][2][1]), as), ws[i][1]);
+            v[i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);  // the GEMM epilogue's mtp_swiglu
+        } else {
+            v[i] = __fadd_rn(xr[i], __fmul_rn(__fmul_rn(comb3(acc[i][0][0], acc[i][1][0], acc[i][2][0]), as), ws[i][0]));
+            x[(size_t)row * d + c] = v[i];
+        }
+        amax = fmaxf(amax, fabsf(v[i]));
+    }
+    // digit planes of the row, as split_digits_kernel
+    amax = block_max(amax, sh);
+    const float mul = (amax == 0.0f || !isfinite(amax)) ? 0.0f : __fdiv_rn(127.0f, amax);
+    const size_t plane = (size_t)M * d;
+#pragma unroll
+    for (int i = 0; i < E; i++) {
+        const int c = t + i * RT;
+        if (c >= d) continue;
+        const float r0 = __fmul_rn(v[i], mul);
+        const float d1 = rintf(r0);
+        const float r1 = __fmul_rn(__fsub_rn(r0, d1), 254.0f);
+        const float d2 = rintf(r1);
+        const float r2 = __fmul_rn(__fsub_rn(r1, d2), 254.0f);
+        const float d3 = fminf(127.0f, fmaxf(-127.0f, rintf(r2)));
+        const size_t o = (size_t)row * d + c;
+        q[o] = (int8_t)(int)d1;
+        q[o + plane] = (int8_t)(int)d2;
+        q[o + 2 * plane] = (int8_t)(int)d3;
+    }
+    if (t == 0) qs[row] = !isfinite(amax) ? __int_as_float(0x7fc00000) : (amax == 0.0f) ? 1.0f : __fdiv_rn(amax, 127.0f);
+}
+
+pf_status mtp_finish(bool swiglu, const int32_t* parts, int n_parts, int64_t part_stride, const float* a_s,
+                     const float* w_s, int d, int M, float* x, int8_t* q, float* qs, cudaStream_t st) {
+    PF_CHECK(d <= RT * 8, "mtp_finish: row length %d above %d", d, RT * 8);
+    PF_CHECK(n_parts >= 1 && n_parts <= kMtpMaxParts &&
+                 part_stride >= (int64_t)3 * M * (swiglu ? 2 * d : d),
+             "mtp_finish: bad slices");
+    PF_CHECK(swiglu || x, "mtp_finish: the residual form needs x");
+    if (swiglu)
+        mtp_finish_kernel<true><<<M, RT, 0, st>>>(parts, n_parts, part_stride, a_s, w_s, d, M, x, q, qs);
+    else
+        mtp_finish_kernel<false><<<M, RT, 0, st>>>(parts, n_parts, part_stride, a_s, w_s, d, M, x, q, qs);
+    return launch_check("mtp_finish");
+}
+
+// ---------------------------------------------------------------------------
 // Tied embedding gather (src/engine.cpp:476-484): x = E[token] * global_scale,
 // zeros for ids outside [0, n_vocab).
 // ---------------------------------------------------------------------------

@@ -19,6 +19,12 @@ pf_status quant_rows(const float* x, int n, int ldx, int M, const int* m_dev, in
                      cudaStream_t st);
 pf_status quant_rows_given(const float* x, int n, int M, const float* s, int8_t* q, float* qs, int ldq,
                            cudaStream_t st);
+// An MTP head projection's finish from K-split slices of its stacked digit-plane
+// rows ([parts][3 M][N]): the GEMM epilogue's arithmetic (SwiGLU over (gate, up)
+// column pairs, N = 2 d; or the residual x += value, N = d), then the three
+// digit planes of the resulting rows into q ([3][M][d]) and qs.
+pf_status mtp_finish(bool swiglu, const int32_t* parts, int n_parts, int64_t part_stride, const float* a_s,
+                     const float* w_s, int d, int M, float* x, int8_t* q, float* qs, cudaStream_t st);
 pf_status split_digits(const float* x, int n, int ldx, int M, const int* m_dev, int8_t* q, int64_t plane,
                        int ldq, float* qs, cudaStream_t st);
 pf_status embed(const int8_t* emb, float gscale, int d, int V, const int* tok, int M, const int* m_dev, float* x,
