@@ -95,7 +95,6 @@ struct pf_engine {
     float* logits = nullptr;
     float* mtp_in = nullptr;   // [max_seqs][d] MTP input (hidden of the row that produced `pending`)
     float* mtp_cur = nullptr;
-    float* mtp_act = nullptr;
     float* mtp_logits = nullptr;
     int* mtp_tok = nullptr;
     int* next = nullptr;
@@ -627,7 +626,6 @@ pf_status pf_engine_create(const pf_model_config* c, int32_t max_seqs, int32_t m
     E_TRY(dalloc(&e->logits, (size_t)e->Mv * V, o));
     E_TRY(dalloc(&e->mtp_in, (size_t)max_seqs * d, o));
     E_TRY(dalloc(&e->mtp_cur, (size_t)max_seqs * d, o));
-    E_TRY(dalloc(&e->mtp_act, (size_t)max_seqs * d, o));
     E_TRY(dalloc(&e->mtp_logits, (size_t)e->K * max_seqs * V, o));
     E_TRY(dalloc(&e->mtp_tok, max_seqs, o));
     E_TRY(dalloc(&e->next, max_seqs, o));
