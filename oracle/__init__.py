@@ -14,7 +14,9 @@ import subprocess
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF_CHECKOUT = os.environ.get("PF_REFERENCE_DIR", "/root/reference")
+# the reference checkout: PF_REFERENCE_DIR, else a "reference" directory beside the repository
+REF_CHECKOUT = os.environ.get("PF_REFERENCE_DIR",
+                              os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _f64p = np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")

@@ -12,7 +12,7 @@
 // (tests/test_oracle_pins.py checks the two bit for bit).
 //
 // The "Level-B" step (the intended batched MTP step) composes the reference's
-// functions with the documented deviations D1-D12 of DESIGN.md:
+// functions with these deviations (D1-D12 in the design notes):
 //   real projection weights, true token positions for RoPE/KV, one K rotation
 //   per kv head, per-head attention output slots, greedy verification with a
 //   commit of the accepted prefix only, and K+1 verify rows [pending, drafts].
