@@ -47,6 +47,22 @@ pf_status dalloc(T** p, size_t n, std::vector<void*>& owned) {
 
 }  // namespace
 
+__global__ void pack_step_kernel(int n, int R, const int* __restrict__ n_emitted, const int* __restrict__ emitted,
+                                 const int* __restrict__ seq_len, const uint32_t* __restrict__ err, int* __restrict__ out) {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        out[i] = n_emitted[i];
+        out[n * (R + 1) + i] = seq_len[i];
+    }
+    for (int i = threadIdx.x; i < n * R; i += blockDim.x) out[n + i] = emitted[i];
+    if (threadIdx.x == 0) out[n * (R + 2)] = err ? (int)*err : 0;
+}
+
+static pf_status pack_step(int n, int R, const int* n_emitted, const int* emitted, const int* seq_len,
+                           const uint32_t* err, int* out, cudaStream_t st) {
+    pack_step_kernel<<<1, 256, 0, st>>>(n, R, n_emitted, emitted, seq_len, err, out);
+    return launch_check("pack_step");
+}
+
 struct pf_engine {
     pf_model_config cfg{};
     int dev = 0;
@@ -131,6 +147,11 @@ struct pf_engine {
     int graph_n = -1;       // sequences the captured step was built for
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     float last_ms = 0.0f;
+    // What the host reads after every step, packed on the device and copied
+    // once into pinned memory by the step graph: [n_emitted n][emitted n R]
+    // [seq_len n][device error flag].
+    int* dpack = nullptr;
+    int* hpin = nullptr;
     // Optional per-kernel timing: event pairs captured into the step graph
     // around every attention (category 0) and projection (category 1) launch.
     static constexpr int kTimedLaunches = 512;
@@ -142,6 +163,7 @@ struct pf_engine {
 
     ~pf_engine() {
         if (graph) cudaGraphExecDestroy(graph);
+        if (hpin) cudaFreeHost(hpin);
         for (cudaEvent_t v : kev) cudaEventDestroy(v);
         if (ev0) cudaEventDestroy(ev0);
         if (ev1) cudaEventDestroy(ev1);
@@ -398,8 +420,13 @@ struct pf_engine {
             PF_TRY(ffn_count(n, L, s.n_commit, ffn_counts, st));
         PF_TRY(gather_rows(x, d, s.final_row, n, mtp_in, st));
         PF_CUDA(cudaMemcpyAsync(mtp_cur, mtp_in, (size_t)n * d * sizeof(float), cudaMemcpyDeviceToDevice, st));
-        return mtp_chain(n);
+        PF_TRY(mtp_chain(n));
+        // the step's results for the host, one copy into pinned memory
+        PF_TRY(pack_step(n, R, sb.n_emitted, sb.emitted, sb.seq_len, device_error_flag(), dpack, st));
+        PF_CUDA(cudaMemcpyAsync(hpin, dpack, pack_bytes(n), cudaMemcpyDeviceToHost, st));
+        return PF_OK;
     }
+    size_t pack_bytes(int n) const { return (size_t)(n * (R + 2) + 1) * sizeof(int); }
 
     pf_status fill_uniforms(int steps);
 };
@@ -654,6 +681,10 @@ pf_status pf_engine_create(const pf_model_config* c, int32_t max_seqs, int32_t m
     E_TRY(dalloc(&sb.final_row, max_seqs, o));
     E_TRY(dalloc(&sb.emitted, (size_t)max_seqs * e->R, o));
     E_TRY(dalloc(&sb.n_emitted, max_seqs, o));
+    E_TRY(dalloc(&e->dpack, (size_t)max_seqs * (e->R + 2) + 1, o));
+    if (cudaHostAlloc(reinterpret_cast<void**>(&e->hpin), ((size_t)max_seqs * (e->R + 2) + 1) * sizeof(int),
+                      cudaHostAllocDefault) != cudaSuccess)
+        return fail(PF_ERR_OOM);
     sb.log_cap = max_positions;
     E_TRY(dalloc(&sb.log, (size_t)max_seqs * max_positions, o));
     E_TRY(dalloc(&sb.n_logged, max_seqs, o));
@@ -1029,21 +1060,30 @@ static pf_status run(pf_engine* e, int steps) {
     return PF_OK;
 }
 
+// After a step graph: the step's packed results from pinned memory (the
+// lengths tighten the host's bound; a latched device error is reported once).
+static pf_status read_pack(pf_engine* e, int32_t* n_emitted, int32_t* emitted) {
+    const int n = e->n_seqs, R = e->R;
+    const int* h = e->hpin;
+    if (n_emitted) std::memcpy(n_emitted, h, (size_t)n * 4);
+    if (emitted) std::memcpy(emitted, h + n, (size_t)n * R * 4);
+    e->host_len.assign(h + n * (R + 1), h + n * (R + 2));
+    const uint32_t flag = (uint32_t)h[n * (R + 2)];
+    if (flag) {
+        cudaMemset(device_error_flag(), 0, 4);
+        set_error("device error flag 0x%x (1 bounds, 2 weight range, 4 token, 8 context full)", flag);
+        return PF_ERR_DEVICE;
+    }
+    return PF_OK;
+}
+
 pf_status pf_engine_step(pf_engine* e, int32_t* n_emitted, int32_t* emitted) {
     PF_CHECK(e, "pf_engine_step: null engine");
     PF_CUDA(cudaSetDevice(e->dev));
     PF_TRY(run(e, 1));
-    if (n_emitted)
-        PF_CUDA(cudaMemcpyAsync(n_emitted, e->sb.n_emitted, e->n_seqs * 4, cudaMemcpyDeviceToHost, e->st));
-    if (emitted)
-        PF_CUDA(cudaMemcpyAsync(emitted, e->sb.emitted, (size_t)e->n_seqs * e->R * 4, cudaMemcpyDeviceToHost, e->st));
     PF_CUDA(cudaStreamSynchronize(e->st));
     PF_CUDA(cudaEventElapsedTime(&e->last_ms, e->ev0, e->ev1));
-    // tighten the host's length bound
-    std::vector<int> len(e->n_seqs);
-    PF_CUDA(cudaMemcpy(len.data(), e->sb.seq_len, e->n_seqs * 4, cudaMemcpyDeviceToHost));
-    e->host_len = len;
-    return read_error_flag(e);
+    return read_pack(e, n_emitted, emitted);
 }
 
 pf_status pf_engine_set_drafts(pf_engine* e, const int32_t* drafts) {
@@ -1064,10 +1104,7 @@ pf_status pf_engine_run_steps(pf_engine* e, int32_t steps) {
     PF_TRY(run(e, steps));
     PF_CUDA(cudaStreamSynchronize(e->st));
     PF_CUDA(cudaEventElapsedTime(&e->last_ms, e->ev0, e->ev1));
-    std::vector<int> len(e->n_seqs);
-    PF_CUDA(cudaMemcpy(len.data(), e->sb.seq_len, e->n_seqs * 4, cudaMemcpyDeviceToHost));
-    e->host_len = len;
-    return read_error_flag(e);
+    return read_pack(e, nullptr, nullptr);
 }
 
 static pf_status d2h(pf_engine* e, void* dst, const void* src, size_t bytes) {
