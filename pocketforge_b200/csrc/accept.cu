@@ -123,7 +123,11 @@ pf_status gather_rows(const float* x, int d, const int* idx, int n, float* out, 
 // rare halfway cases); the normalising sum and the cumulative scans are
 // sequential float additions in the reference's order, so the draw is the
 // reference's.  Sorted-descending scans stop at the first zero term (adding
-// +0 changes nothing).
+// +0 changes nothing).  The divisions by the sum are independent of one
+// another and run on all threads; one thread then adds the quotients in
+// order, and a single pass finds both the draw and the top-p cut (the
+// reference's two cumulative scans add the same quotients in the same
+// order, so their partial sums are the same numbers).
 // ---------------------------------------------------------------------------
 namespace {
 constexpr int SORT_THREADS = 1024;
@@ -167,11 +171,19 @@ __global__ void __launch_bounds__(SORT_THREADS) sample_kernel(const float* __res
         __syncthreads();
         if (tid == 0) {
             float sum = 0.0f;
+#pragma unroll 8
             for (int i = 0; i < V; i++) sum = __fadd_rn(sum, key[i]);
+            red[0] = sum;
+        }
+        __syncthreads();
+        const float sum = red[0];
+        for (int i = tid; i < V; i += blockDim.x) key[i] = __fdiv_rn(key[i], sum);
+        __syncthreads();
+        if (tid == 0) {
             float cum = 0.0f;
             int pick = V - 1;
             for (int i = 0; i < V; i++) {
-                cum = __fadd_rn(cum, __fdiv_rn(key[i], sum));
+                cum = __fadd_rn(cum, key[i]);
                 if (u <= cum) {
                     pick = i;
                     break;
@@ -211,32 +223,40 @@ __global__ void __launch_bounds__(SORT_THREADS) sample_kernel(const float* __res
     // exponentials in sorted order, in place (key[i] is no longer needed after this)
     for (int i = tid; i < nn; i += blockDim.x) key[i] = exp_ref(__fdiv_rn(__fsub_rn(key[i], mx), t));
     __syncthreads();
-    if (tid != 0) return;
-    float total = 0.0f;
-    int nz = nn;  // terms after the first zero are zero too (sorted descending)
-    for (int i = 0; i < nn; i++) {
-        if (key[i] == 0.0f) {
-            nz = i;
-            break;
-        }
-        total = __fadd_rn(total, key[i]);
-    }
-    if (top_p) {  // src/engine.cpp:972-1002: normalise, cut at cumulative >= p, draw without renormalising
-        int cut = nn;
-        float cum = 0.0f;
-        for (int i = 0; i < nz; i++) {
-            cum = __fadd_rn(cum, __fdiv_rn(key[i], total));
-            if (cum >= cfg.top_p) {
-                cut = i + 1;
+    __shared__ int s_nz;
+    if (tid == 0) {
+        float total = 0.0f;
+        int nz = nn;  // terms after the first zero are zero too (sorted descending)
+        for (int i = 0; i < nn; i++) {
+            if (key[i] == 0.0f) {
+                nz = i;
                 break;
             }
+            total = __fadd_rn(total, key[i]);
         }
-        cum = 0.0f;
+        red[0] = total;
+        s_nz = nz;
+    }
+    __syncthreads();
+    const float total = red[0];
+    const int nz = s_nz;
+    for (int i = tid; i < nz; i += blockDim.x) key[i] = __fdiv_rn(key[i], total);  // the normalised terms
+    __syncthreads();
+    if (tid != 0) return;
+    if (top_p) {  // src/engine.cpp:972-1002: normalise, cut at cumulative >= p, draw without renormalising
+        // The draw scans i < min(cut, nz) with the same partial sums as the
+        // cut scan: checking the draw before the cut at each i is both scans.
+        int cut = nn;
+        float cum = 0.0f;
         int pick = -1;
-        for (int i = 0; i < min(cut, nz); i++) {
-            cum = __fadd_rn(cum, __fdiv_rn(key[i], total));
+        for (int i = 0; i < nz; i++) {
+            cum = __fadd_rn(cum, key[i]);
             if (u <= cum) {
                 pick = i;
+                break;
+            }
+            if (cum >= cfg.top_p) {
+                cut = i + 1;
                 break;
             }
         }
@@ -245,7 +265,7 @@ __global__ void __launch_bounds__(SORT_THREADS) sample_kernel(const float* __res
         float cum = 0.0f;
         int pick = -1;
         for (int i = 0; i < nz; i++) {
-            cum = __fadd_rn(cum, __fdiv_rn(key[i], total));
+            cum = __fadd_rn(cum, key[i]);
             if (u <= cum) {
                 pick = i;
                 break;
@@ -307,9 +327,21 @@ __global__ void skip_decide_kernel(int nb, const int* __restrict__ bs_row0, cons
     for (int r = 0; r < n; r++) {
         const float* x = normed + (size_t)(row0 + r) * d;
         float s = 0.0f;
-        for (int i = lane; i < d; i += 32) {
-            const float df = __fsub_rn(x[i], ref[i]);
-            s = __fadd_rn(s, __fmul_rn(df, df));
+        // the lane's elements in order, 16 at a time with their loads issued first
+        for (int i0 = lane; i0 < d; i0 += 32 * 16) {
+            float xa[16], ra[16];
+#pragma unroll
+            for (int k = 0; k < 16; k++) {
+                const int i = i0 + 32 * k;
+                xa[k] = i < d ? x[i] : 0.0f;
+                ra[k] = i < d ? ref[i] : 0.0f;
+            }
+#pragma unroll
+            for (int k = 0; k < 16; k++) {
+                if (i0 + 32 * k >= d) break;
+                const float df = __fsub_rn(xa[k], ra[k]);
+                s = __fadd_rn(s, __fmul_rn(df, df));
+            }
         }
         for (int o = 16; o >= 1; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
         const float delta = __fsqrt_rn(__fdiv_rn(s, (float)d));
