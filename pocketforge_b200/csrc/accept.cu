@@ -136,6 +136,26 @@ __device__ __forceinline__ bool before(float va, int ia, float vb, int ib) {
     return va > vb || (va == vb && ia < ib);
 }
 __device__ __forceinline__ float exp_ref(float x) { return (float)exp((double)x); }
+
+// One thread's ordered pass over a[0, n): f(i, a[i]) for i = 0, 1, ... until
+// it returns true; returns that i, or n.  Four terms per 16-byte load, the
+// next four loaded before the current ones are used (a is 16-byte aligned).
+template <typename F>
+__device__ __forceinline__ int ordered_pass(const float* a, int n, F f) {
+    const int n4 = n & ~3;
+    float4 nxt = n4 > 0 ? *reinterpret_cast<const float4*>(a) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = 0; i < n4; i += 4) {
+        const float4 v = nxt;
+        if (i + 4 < n4) nxt = *reinterpret_cast<const float4*>(a + i + 4);
+        if (f(i, v.x)) return i;
+        if (f(i + 1, v.y)) return i + 1;
+        if (f(i + 2, v.z)) return i + 2;
+        if (f(i + 3, v.w)) return i + 3;
+    }
+    for (int i = n4; i < n; i++)
+        if (f(i, a[i])) return i;
+    return n;
+}
 }  // namespace
 
 __global__ void __launch_bounds__(SORT_THREADS) sample_kernel(const float* __restrict__ logits, int ld, int V, int P2,
@@ -171,8 +191,10 @@ __global__ void __launch_bounds__(SORT_THREADS) sample_kernel(const float* __res
         __syncthreads();
         if (tid == 0) {
             float sum = 0.0f;
-#pragma unroll 8
-            for (int i = 0; i < V; i++) sum = __fadd_rn(sum, key[i]);
+            ordered_pass(key, V, [&](int, float q) {
+                sum = __fadd_rn(sum, q);
+                return false;
+            });
             red[0] = sum;
         }
         __syncthreads();
@@ -181,15 +203,11 @@ __global__ void __launch_bounds__(SORT_THREADS) sample_kernel(const float* __res
         __syncthreads();
         if (tid == 0) {
             float cum = 0.0f;
-            int pick = V - 1;
-            for (int i = 0; i < V; i++) {
-                cum = __fadd_rn(cum, key[i]);
-                if (u <= cum) {
-                    pick = i;
-                    break;
-                }
-            }
-            out[b] = pick;
+            const int i = ordered_pass(key, V, [&](int, float q) {
+                cum = __fadd_rn(cum, q);
+                return u <= cum;
+            });
+            out[b] = i < V ? i : V - 1;
         }
         return;
     }
@@ -226,14 +244,12 @@ __global__ void __launch_bounds__(SORT_THREADS) sample_kernel(const float* __res
     __shared__ int s_nz;
     if (tid == 0) {
         float total = 0.0f;
-        int nz = nn;  // terms after the first zero are zero too (sorted descending)
-        for (int i = 0; i < nn; i++) {
-            if (key[i] == 0.0f) {
-                nz = i;
-                break;
-            }
-            total = __fadd_rn(total, key[i]);
-        }
+        // terms after the first zero are zero too (sorted descending)
+        const int nz = ordered_pass(key, nn, [&](int, float q) {
+            if (q == 0.0f) return true;
+            total = __fadd_rn(total, q);
+            return false;
+        });
         red[0] = total;
         s_nz = nz;
     }
@@ -249,29 +265,26 @@ __global__ void __launch_bounds__(SORT_THREADS) sample_kernel(const float* __res
         int cut = nn;
         float cum = 0.0f;
         int pick = -1;
-        for (int i = 0; i < nz; i++) {
-            cum = __fadd_rn(cum, key[i]);
+        ordered_pass(key, nz, [&](int i, float q) {
+            cum = __fadd_rn(cum, q);
             if (u <= cum) {
                 pick = i;
-                break;
+                return true;
             }
             if (cum >= cfg.top_p) {
                 cut = i + 1;
-                break;
+                return true;
             }
-        }
+            return false;
+        });
         out[b] = idx[pick >= 0 ? pick : cut - 1];
     } else {  // top-k (src/engine.cpp:930-959)
         float cum = 0.0f;
-        int pick = -1;
-        for (int i = 0; i < nz; i++) {
-            cum = __fadd_rn(cum, key[i]);
-            if (u <= cum) {
-                pick = i;
-                break;
-            }
-        }
-        out[b] = idx[pick >= 0 ? pick : nn - 1];
+        const int i = ordered_pass(key, nz, [&](int, float q) {
+            cum = __fadd_rn(cum, q);
+            return u <= cum;
+        });
+        out[b] = idx[i < nz ? i : nn - 1];
     }
 }
 
