@@ -75,7 +75,10 @@ PRESETS = {
     # configs of the reference's benchmark description (model dims shared)
     "config1": dict(model=replace(BASE_1B, window_size=2048), seqs=1, prompt=128, gen=256),
     "config2": dict(model=replace(BASE_1B, window_size=8192, max_context=8192), seqs=64, prompt=512, gen=512),
-    "config3": dict(model=replace(BASE_1B, window_size=4096), seqs=16, prompt=131072, gen=512),
+    # positions >= max_context are not stored: room for the 512 generated
+    # tokens and the verify rows after the 131072-token prompt
+    "config3": dict(model=replace(BASE_1B, window_size=4096, max_context=131072 + 4096), seqs=16, prompt=131072,
+                    gen=512),
     "config4": dict(model=replace(BASE_1B, qtype=[QT_Q4, QT_Q4, QT_Q4, QT_Q4, QT_Q2, QT_Q2, QT_Q15],
                                   skip_enabled=True), seqs=128, prompt=256, gen=256,
                     sampling=dict(temperature=0.8, top_k=40, top_p=0.95, seed=2)),

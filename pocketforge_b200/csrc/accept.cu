@@ -117,55 +117,177 @@ pf_status gather_rows(const float* x, int d, const int* idx, int n, float* out, 
 // Dispatch as the reference: top-p when 0<p<1 (top-k is then ignored),
 // else top-k when 0<k<V, else plain temperature.  One CTA sorts the row
 // (descending value, ascending index on ties; std::sort leaves the order of
-// exactly equal logits unspecified) with a bitonic sort in shared memory.
-// The exponentials are computed in parallel (double exp rounded to float:
-// the correctly rounded value the reference's std::exp returns in all but
-// rare halfway cases); the normalising sum and the cumulative scans are
-// sequential float additions in the reference's order, so the draw is the
-// reference's.  Sorted-descending scans stop at the first zero term (adding
-// +0 changes nothing).  The divisions by the sum are independent of one
-// another and run on all threads; one thread then adds the quotients in
-// order, and a single pass finds both the draw and the top-p cut (the
-// reference's two cumulative scans add the same quotients in the same
-// order, so their partial sums are the same numbers).
+// exactly equal logits unspecified) with a stable radix sort in shared
+// memory.  The exponentials are computed in parallel (double exp rounded to
+// float: the correctly rounded value the reference's std::exp returns in all
+// but rare halfway cases) and so are the divisions by the sum; the
+// normalising sum and the cumulative scan are sequential float additions in
+// the reference's order, so the draw is the reference's.  One cumulative scan
+// finds both the draw and the top-p cut: the reference's two cumulative scans
+// add the same quotients in the same order, so their partial sums are the
+// same numbers, and whichever stops first decides the token.
 // ---------------------------------------------------------------------------
 namespace {
 constexpr int SORT_THREADS = 1024;
+constexpr int SORT_WARPS = SORT_THREADS / 32;
+constexpr int SORT_IPT = 16;  // items per thread: rows of up to 16384 entries
+constexpr int SORT_RADIX = 256;
 
-__device__ __forceinline__ bool before(float va, int ia, float vb, int ib) {
-    return va > vb || (va == vb && ia < ib);
-}
 __device__ __forceinline__ float exp_ref(float x) { return (float)exp((double)x); }
 
-// One thread's ordered pass over a[0, n): f(i, a[i]) for i = 0, 1, ... until
-// it returns true; returns that i, or n.  Four terms per 16-byte load, the
-// next four loaded before the current ones are used (a is 16-byte aligned).
-template <typename F>
-__device__ __forceinline__ int ordered_pass(const float* a, int n, F f) {
-    const int n4 = n & ~3;
-    float4 nxt = n4 > 0 ? *reinterpret_cast<const float4*>(a) : make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int i = 0; i < n4; i += 4) {
-        const float4 v = nxt;
-        if (i + 4 < n4) nxt = *reinterpret_cast<const float4*>(a + i + 4);
-        if (f(i, v.x)) return i;
-        if (f(i + 1, v.y)) return i + 1;
-        if (f(i + 2, v.z)) return i + 2;
-        if (f(i + 3, v.w)) return i + 3;
+// Sort key whose ascending unsigned order is descending value; -0 and +0 get
+// the same key (they compare equal, and every use of the value gives the same
+// result for either sign).
+__device__ __forceinline__ uint32_t desc_key(float v) {
+    uint32_t b = __float_as_uint(v == 0.0f ? 0.0f : v);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ~b;
+}
+__device__ __forceinline__ float key_value(uint32_t k) {
+    const uint32_t b = ~k;
+    return __uint_as_float((b & 0x80000000u) ? (b & 0x7fffffffu) : ~b);
+}
+
+// Stable ascending LSD radix sort (8-bit digits) of the CTA's R*1024 items.
+// Item j = w*32R + r*32 + lane sits in k[r] / pv[r] >> 16 of that lane of
+// warp w; the sorted keys and payloads end in ks / vs.  Ranks within a warp
+// come from __match_any_sync in item order; warps' digit counts are scanned
+// digit-major, warp-minor, so equal digits keep their item order (stability).
+// The payload (< 65536) sits in pv's high half; the low half holds the item's
+// rank among the warp's items of its digit during a pass.
+__device__ __forceinline__ void block_radix_sort(uint32_t (&k)[SORT_IPT], uint32_t (&pv)[SORT_IPT], int R,
+                                                 uint32_t* ks, uint32_t* vs, uint32_t* hist, uint32_t* wsum) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const uint32_t lt = (1u << lane) - 1u;
+    uint32_t* hw = hist + w * SORT_RADIX;
+    for (int sh = 0; sh < 32; sh += 8) {
+        for (int d = lane; d < SORT_RADIX; d += 32) hw[d] = 0;
+        __syncwarp();
+#pragma unroll
+        for (int r = 0; r < SORT_IPT; r++) {
+            if (r < R) {
+                const uint32_t d = (k[r] >> sh) & (SORT_RADIX - 1);
+                const uint32_t peers = __match_any_sync(0xffffffffu, d);
+                const uint32_t base = hw[d];
+                __syncwarp();
+                if ((peers & lt) == 0) hw[d] = base + __popc(peers);
+                __syncwarp();
+                pv[r] = (pv[r] & 0xffff0000u) | (base + __popc(peers & lt));
+            }
+        }
+        __syncthreads();
+        {  // exclusive scan of the counts in (digit, warp) order: thread t owns digit t/4, warps (t%4)*8 ..
+            const int d = threadIdx.x >> 2, w0 = (threadIdx.x & 3) * 8;
+            uint32_t c[8], s = 0;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                c[j] = hist[(w0 + j) * SORT_RADIX + d];
+                s += c[j];
+            }
+            uint32_t incl = s;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            if (lane == 31) wsum[w] = incl;
+            __syncthreads();
+            if (w == 0) {
+                const uint32_t x = wsum[lane];
+                uint32_t xi = x;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const uint32_t y = __shfl_up_sync(0xffffffffu, xi, o);
+                    if (lane >= o) xi += y;
+                }
+                wsum[lane] = xi - x;
+            }
+            __syncthreads();
+            uint32_t run = wsum[w] + incl - s;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                hist[(w0 + j) * SORT_RADIX + d] = run;
+                run += c[j];
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int r = 0; r < SORT_IPT; r++) {
+            if (r < R) {
+                const uint32_t dst = hw[(k[r] >> sh) & (SORT_RADIX - 1)] + (pv[r] & 0xffffu);
+                ks[dst] = k[r];
+                vs[dst] = pv[r] >> 16;
+            }
+        }
+        __syncthreads();
+        if (sh == 24) break;
+#pragma unroll
+        for (int r = 0; r < SORT_IPT; r++) {
+            if (r < R) {
+                const int j = w * 32 * R + r * 32 + lane;
+                k[r] = ks[j];
+                pv[r] = vs[j] << 16;
+            }
+        }
     }
-    for (int i = n4; i < n; i++)
-        if (f(i, a[i])) return i;
+}
+
+// One thread's cumulative float sum of a[0, n) in index order, continuing
+// from cum.  Returns the first i whose partial sum c satisfies stop(c) (cum is
+// then that sum), else n (cum is the full sum).  The terms are >= 0, so the
+// partial sums never decrease and stop (monotone in c) is checked once per 16
+// terms; only the group that holds the stop is walked again.  Sixteen terms
+// are loaded ahead of the adds that use them (a is 16-byte aligned).
+template <typename Stop>
+__device__ __forceinline__ int ordered_scan(const float* a, int n, float& cum, Stop stop) {
+    const int n16 = n & ~15;
+    const float4* a4 = reinterpret_cast<const float4*>(a);
+    float4 q[4];
+    if (n16 > 0)
+#pragma unroll
+        for (int j = 0; j < 4; j++) q[j] = a4[j];
+    for (int i = 0; i < n16; i += 16) {
+        const float t[16] = {q[0].x, q[0].y, q[0].z, q[0].w, q[1].x, q[1].y, q[1].z, q[1].w,
+                             q[2].x, q[2].y, q[2].z, q[2].w, q[3].x, q[3].y, q[3].z, q[3].w};
+        if (i + 16 < n16)
+#pragma unroll
+            for (int j = 0; j < 4; j++) q[j] = a4[(i >> 2) + 4 + j];
+        float s[16];
+        float c = cum;
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            c = __fadd_rn(c, t[j]);
+            s[j] = c;
+        }
+        if (stop(c)) {
+#pragma unroll
+            for (int j = 0; j < 16; j++)
+                if (stop(s[j])) {
+                    cum = s[j];
+                    return i + j;
+                }
+        }
+        cum = c;
+    }
+    for (int i = n16; i < n; i++) {
+        cum = __fadd_rn(cum, a[i]);
+        if (stop(cum)) return i;
+    }
     return n;
 }
 }  // namespace
 
-__global__ void __launch_bounds__(SORT_THREADS) sample_kernel(const float* __restrict__ logits, int ld, int V, int P2,
-                                                              const int* __restrict__ rows, int n, pf_sampling_config cfg,
-                                                              const float* __restrict__ uniforms, int ustride,
-                                                              int* __restrict__ out) {
+__global__ void __launch_bounds__(SORT_THREADS, 1)
+    sample_kernel(const float* __restrict__ logits, int ld, int V, int R, const int* __restrict__ rows, int n,
+                  pf_sampling_config cfg, const float* __restrict__ uniforms, int ustride, int* __restrict__ out) {
     extern __shared__ __align__(16) uint8_t sm[];
-    float* key = reinterpret_cast<float*>(sm);
-    int* idx = reinterpret_cast<int*>(sm + (size_t)P2 * sizeof(float));
-    __shared__ float red[32];
+    const int cap = R * SORT_THREADS;
+    uint32_t* ks = reinterpret_cast<uint32_t*>(sm);
+    uint32_t* vs = ks + cap;
+    uint32_t* hist = vs + cap;
+    float* key = reinterpret_cast<float*>(sm);  // values / terms, in place of ks
+    __shared__ float red[SORT_WARPS];
+    __shared__ uint32_t wsum[SORT_WARPS];
     const int b = blockIdx.x;
     if (b >= n) return;
     const float* lg = logits + (size_t)rows[b] * ld;
@@ -182,7 +304,7 @@ __global__ void __launch_bounds__(SORT_THREADS) sample_kernel(const float* __res
         __syncthreads();
         if (tid == 0) {
             float m = red[0];
-            for (int w = 1; w < (int)(blockDim.x >> 5); w++) m = fmaxf(m, red[w]);
+            for (int w = 1; w < SORT_WARPS; w++) m = fmaxf(m, red[w]);
             red[0] = m;
         }
         __syncthreads();
@@ -191,115 +313,79 @@ __global__ void __launch_bounds__(SORT_THREADS) sample_kernel(const float* __res
         __syncthreads();
         if (tid == 0) {
             float sum = 0.0f;
-            ordered_pass(key, V, [&](int, float q) {
-                sum = __fadd_rn(sum, q);
-                return false;
-            });
-            red[0] = sum;
+            ordered_scan(key, V, sum, [](float) { return false; });
+            red[1] = sum;
         }
         __syncthreads();
-        const float sum = red[0];
+        const float sum = red[1];
         for (int i = tid; i < V; i += blockDim.x) key[i] = __fdiv_rn(key[i], sum);
         __syncthreads();
         if (tid == 0) {
             float cum = 0.0f;
-            const int i = ordered_pass(key, V, [&](int, float q) {
-                cum = __fadd_rn(cum, q);
-                return u <= cum;
-            });
+            const int i = ordered_scan(key, V, cum, [u](float c) { return u <= c; });
             out[b] = i < V ? i : V - 1;
         }
         return;
     }
-    for (int i = tid; i < P2; i += blockDim.x) {
-        key[i] = i < V ? lg[i] : -INFINITY;
-        idx[i] = i < V ? i : 0x7fffffff;
-    }
-    __syncthreads();
-    for (int k = 2; k <= P2; k <<= 1)
-        for (int j = k >> 1; j > 0; j >>= 1) {
-            for (int i = tid; i < P2; i += blockDim.x) {
-                const int p = i ^ j;
-                if (p > i) {
-                    const bool desc = (i & k) == 0;
-                    const bool swap = desc ? before(key[p], idx[p], key[i], idx[i]) : before(key[i], idx[i], key[p], idx[p]);
-                    if (swap) {
-                        const float tk = key[i];
-                        key[i] = key[p];
-                        key[p] = tk;
-                        const int ti = idx[i];
-                        idx[i] = idx[p];
-                        idx[p] = ti;
-                    }
-                }
+    {
+        const int lane = tid & 31, w = tid >> 5;
+        uint32_t k[SORT_IPT], pv[SORT_IPT];
+#pragma unroll
+        for (int r = 0; r < SORT_IPT; r++) {
+            if (r < R) {
+                const int j = w * 32 * R + r * 32 + lane;
+                k[r] = j < V ? desc_key(lg[j]) : 0xffffffffu;  // padding sorts after every real entry
+                pv[r] = (uint32_t)(j < V ? j : 0xffff) << 16;
             }
-            __syncthreads();
         }
-    const float mx = key[0];
+        block_radix_sort(k, pv, R, ks, vs, hist, wsum);
+    }
+    const float mx = key_value(ks[0]);
     const int nn = top_p ? V : (int)cfg.top_k;
     __syncthreads();
-    // exponentials in sorted order, in place (key[i] is no longer needed after this)
-    for (int i = tid; i < nn; i += blockDim.x) key[i] = exp_ref(__fdiv_rn(__fsub_rn(key[i], mx), t));
+    // exponentials in sorted order, in place of the keys
+    for (int i = tid; i < nn; i += blockDim.x) key[i] = exp_ref(__fdiv_rn(__fsub_rn(key_value(ks[i]), mx), t));
     __syncthreads();
-    __shared__ int s_nz;
     if (tid == 0) {
+        // terms after the first zero are zero too (sorted descending) and add nothing
         float total = 0.0f;
-        // terms after the first zero are zero too (sorted descending)
-        const int nz = ordered_pass(key, nn, [&](int, float q) {
-            if (q == 0.0f) return true;
-            total = __fadd_rn(total, q);
-            return false;
-        });
+        ordered_scan(key, nn, total, [](float) { return false; });
         red[0] = total;
-        s_nz = nz;
     }
     __syncthreads();
     const float total = red[0];
-    const int nz = s_nz;
-    for (int i = tid; i < nz; i += blockDim.x) key[i] = __fdiv_rn(key[i], total);  // the normalised terms
+    for (int i = tid; i < nn; i += blockDim.x) key[i] = __fdiv_rn(key[i], total);  // the normalised terms
     __syncthreads();
     if (tid != 0) return;
-    if (top_p) {  // src/engine.cpp:972-1002: normalise, cut at cumulative >= p, draw without renormalising
-        // The draw scans i < min(cut, nz) with the same partial sums as the
-        // cut scan: checking the draw before the cut at each i is both scans.
-        int cut = nn;
-        float cum = 0.0f;
-        int pick = -1;
-        ordered_pass(key, nz, [&](int i, float q) {
-            cum = __fadd_rn(cum, q);
-            if (u <= cum) {
-                pick = i;
-                return true;
-            }
-            if (cum >= cfg.top_p) {
-                cut = i + 1;
-                return true;
-            }
-            return false;
-        });
-        out[b] = idx[pick >= 0 ? pick : cut - 1];
+    float cum = 0.0f;
+    int i;
+    if (top_p) {
+        // src/engine.cpp:972-1002: normalise, cut at cumulative >= p, draw
+        // without renormalising.  The draw stops at the first u <= cum; the cut
+        // at the first cum >= p keeps entries 0..i, and a draw that found no
+        // entry by then takes the last kept one, entry i.  Either way the
+        // token is the entry where the first of the two holds.
+        const float p = cfg.top_p;
+        i = ordered_scan(key, nn, cum, [u, p](float c) { return u <= c || c >= p; });
     } else {  // top-k (src/engine.cpp:930-959)
-        float cum = 0.0f;
-        const int i = ordered_pass(key, nz, [&](int, float q) {
-            cum = __fadd_rn(cum, q);
-            return u <= cum;
-        });
-        out[b] = idx[i < nz ? i : nn - 1];
+        i = ordered_scan(key, nn, cum, [u](float c) { return u <= c; });
     }
+    out[b] = (int)vs[i < nn ? i : nn - 1];
 }
 
 pf_status sample_rows(const float* logits, int ld, int V, const int* rows, int n, const pf_sampling_config& cfg,
                       const float* uniforms, int ustride, int* out, cudaStream_t st) {
-    int P2 = 1;
-    while (P2 < V) P2 <<= 1;
-    PF_CHECK(P2 <= 16384, "sample_rows: vocabulary above 16384 is not supported");
-    const size_t smem = (size_t)P2 * (sizeof(float) + sizeof(int));
+    PF_CHECK(V >= 1 && V <= SORT_THREADS * SORT_IPT, "sample_rows: vocabulary above 16384 is not supported");
+    const int R = (V + SORT_THREADS - 1) / SORT_THREADS;
+    const size_t smem = (size_t)R * SORT_THREADS * 2 * sizeof(uint32_t) + SORT_WARPS * SORT_RADIX * sizeof(uint32_t);
     static bool attr = false;
     if (!attr) {
-        PF_CUDA(cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 16384 * 8));
+        PF_CUDA(cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     SORT_THREADS * SORT_IPT * 2 * sizeof(uint32_t) +
+                                         SORT_WARPS * SORT_RADIX * sizeof(uint32_t)));
         attr = true;
     }
-    sample_kernel<<<n, SORT_THREADS, smem, st>>>(logits, ld, V, P2, rows, n, cfg, uniforms, ustride, out);
+    sample_kernel<<<n, SORT_THREADS, smem, st>>>(logits, ld, V, R, rows, n, cfg, uniforms, ustride, out);
     return launch_check("sample_rows");
 }
 
@@ -327,8 +413,43 @@ pf_status put_draft(const int* tok, int n, int K, int h, int* drafts, cudaStream
 // Predictive FFN skip (LayerSkipController::should_skip_ffn,
 // src/layer_skip.cpp:22-67): rows of a sequence in order, each compared with
 // the post-norm vector of the last row whose FFN ran (committed cache at the
-// start).  One warp per sequence; the RMS delta uses the device sum order.
+// start); the row skips when the RMS of the difference is below the layer's
+// threshold.  The RMS delta uses the device sum order below.
 // ---------------------------------------------------------------------------
+namespace {
+// One warp's sum of (x - ref)^2 over d: each lane adds its elements
+// lane, lane+32, ... in order (loads issued 16 at a time ahead of the adds),
+// then a butterfly over the lanes.  Every caller uses this order, so a
+// difference computed twice is the same number.
+__device__ __forceinline__ float warp_sqdiff(const float* __restrict__ x, const float* __restrict__ ref, int d,
+                                             int lane) {
+    float s = 0.0f;
+    for (int i0 = lane; i0 < d; i0 += 32 * 16) {
+        float xa[16], ra[16];
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            const int i = i0 + 32 * k;
+            xa[k] = i < d ? x[i] : 0.0f;
+            ra[k] = i < d ? ref[i] : 0.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            if (i0 + 32 * k >= d) break;
+            const float df = __fsub_rn(xa[k], ra[k]);
+            s = __fadd_rn(s, __fmul_rn(df, df));
+        }
+    }
+    for (int o = 16; o >= 1; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+    return s;
+}
+__device__ __forceinline__ bool skip_rule(float s, int d, float thr_l) {
+    return __fsqrt_rn(__fdiv_rn(s, (float)d)) < thr_l;
+}
+constexpr int SKIP_PAIR_ROWS = 9;  // rows per sequence of the pairwise form (K + 1 for K <= 8)
+constexpr int SKIP_PAIR_WARPS = 16;
+}  // namespace
+
+// Long row batches (prefill chunks): one warp per sequence walks its rows.
 __global__ void skip_decide_kernel(int nb, const int* __restrict__ bs_row0, const int* __restrict__ bs_n,
                                    const float* __restrict__ normed, int d, const float* __restrict__ cache,
                                    size_t cache_stride, float thr_l, uint8_t* __restrict__ skip) {
@@ -339,35 +460,56 @@ __global__ void skip_decide_kernel(int nb, const int* __restrict__ bs_row0, cons
     const float* ref = cache + (size_t)b * cache_stride;
     for (int r = 0; r < n; r++) {
         const float* x = normed + (size_t)(row0 + r) * d;
-        float s = 0.0f;
-        // the lane's elements in order, 16 at a time with their loads issued first
-        for (int i0 = lane; i0 < d; i0 += 32 * 16) {
-            float xa[16], ra[16];
-#pragma unroll
-            for (int k = 0; k < 16; k++) {
-                const int i = i0 + 32 * k;
-                xa[k] = i < d ? x[i] : 0.0f;
-                ra[k] = i < d ? ref[i] : 0.0f;
-            }
-#pragma unroll
-            for (int k = 0; k < 16; k++) {
-                if (i0 + 32 * k >= d) break;
-                const float df = __fsub_rn(xa[k], ra[k]);
-                s = __fadd_rn(s, __fmul_rn(df, df));
-            }
-        }
-        for (int o = 16; o >= 1; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
-        const float delta = __fsqrt_rn(__fdiv_rn(s, (float)d));
-        const bool sk = delta < thr_l;
+        const bool sk = skip_rule(warp_sqdiff(x, ref, d, lane), d, thr_l);
         if (lane == 0) skip[row0 + r] = sk ? 1 : 0;
         if (!sk) ref = x;
     }
 }
 
-pf_status skip_decide(int nb, const int* bs_row0, const int* bs_n, const float* normed, int d, const float* cache,
-                      size_t cache_stride, float thr_l, uint8_t* skip, cudaStream_t st) {
-    skip_decide_kernel<<<ceil_div(nb, 4), 128, 0, st>>>(nb, bs_row0, bs_n, normed, d, cache, cache_stride, thr_l,
-                                                        skip);
+// Verify steps (at most SKIP_PAIR_ROWS rows per sequence): the reference row
+// of row r is the cache or one of rows 0..r-1, so the r+1 candidate
+// differences of every row are computed at once, one warp per (row, candidate)
+// pair, and one thread then walks the rows through that table.  Same sums and
+// same decisions as the walk above, without the rows waiting on each other.
+__global__ void __launch_bounds__(SKIP_PAIR_WARPS * 32)
+    skip_decide_pairs_kernel(const int* __restrict__ bs_row0, const int* __restrict__ bs_n,
+                             const float* __restrict__ normed, int d, const float* __restrict__ cache,
+                             size_t cache_stride, float thr_l, uint8_t* __restrict__ skip) {
+    __shared__ uint8_t tab[SKIP_PAIR_ROWS * (SKIP_PAIR_ROWS + 1) / 2];
+    const int b = blockIdx.x;
+    const int n = min(bs_n[b], SKIP_PAIR_ROWS), row0 = bs_row0[b];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const float* c = cache + (size_t)b * cache_stride;
+    // pair index of (row r, candidate j): r(r+1)/2 + j, j = 0 the cache, j >= 1 row j-1
+    for (int pr = w; pr < n * (n + 1) / 2; pr += SKIP_PAIR_WARPS) {
+        int r = 0;
+        while ((r + 1) * (r + 2) / 2 <= pr) r++;
+        const int j = pr - r * (r + 1) / 2;
+        const float* x = normed + (size_t)(row0 + r) * d;
+        const float* ref = j == 0 ? c : normed + (size_t)(row0 + j - 1) * d;
+        const bool sk = skip_rule(warp_sqdiff(x, ref, d, lane), d, thr_l);
+        if (lane == 0) tab[pr] = sk ? 1 : 0;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int j = 0;
+        for (int r = 0; r < n; r++) {
+            const bool sk = tab[r * (r + 1) / 2 + j] != 0;
+            skip[row0 + r] = sk ? 1 : 0;
+            if (!sk) j = r + 1;
+        }
+    }
+}
+
+pf_status skip_decide(int nb, const int* bs_row0, const int* bs_n, int max_rows, const float* normed, int d,
+                      const float* cache, size_t cache_stride, float thr_l, uint8_t* skip, cudaStream_t st) {
+    if (nb <= 0) return PF_OK;
+    if (max_rows <= SKIP_PAIR_ROWS)
+        skip_decide_pairs_kernel<<<nb, SKIP_PAIR_WARPS * 32, 0, st>>>(bs_row0, bs_n, normed, d, cache, cache_stride,
+                                                                       thr_l, skip);
+    else
+        skip_decide_kernel<<<ceil_div(nb, 4), 128, 0, st>>>(nb, bs_row0, bs_n, normed, d, cache, cache_stride, thr_l,
+                                                            skip);
     return launch_check("skip_decide");
 }
 

@@ -309,8 +309,8 @@ struct pf_engine {
             uint8_t* skipl = skip_on ? skip_all + (size_t)l * sM : nullptr;
             PF_TRY(norm_rows(&pend, ffn_norm + (size_t)l * d, M, normed));
             if (skip_on)
-                PF_TRY(skip_decide(rb.nb, rb.row0, rb.n, normed, d, skip_cache + (size_t)l * d, (size_t)L * d,
-                                   layer_threshold(l), skipl, st));
+                PF_TRY(skip_decide(rb.nb, rb.row0, rb.n, rb.max_rows, normed, d, skip_cache + (size_t)l * d,
+                                   (size_t)L * d, layer_threshold(l), skipl, st));
             {
                 GemmParams p;
                 p.A = xq; p.lda = d; p.a_scale = xs; p.M = M; p.N = 2 * F; p.K = d;

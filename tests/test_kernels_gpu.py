@@ -186,15 +186,23 @@ def test_argmax_first_max(olib):
     assert got[3] == 10 and got[4] == 0 and got[5] == n - 1
 
 
+@pytest.mark.parametrize("shape", ["full", "ties", "ragged"])
 @pytest.mark.parametrize("mode", ["top_p", "top_k", "temp"])
-def test_sampling_matches_oracle(olib, mode):
-    """Same logits and uniform draws: the sampled token must agree except where
-    the draw falls within float rounding of a cumulative boundary (the GPU sums
-    in double, the reference in float).  Tolerance: >= 99% agreement."""
+def test_sampling_matches_oracle(olib, mode, shape):
+    """Same logits and uniform draws: the sampled token must agree.  The sums
+    are the reference's float sums in its order; the exponentials are double
+    exp rounded to float, which can differ from the C library's float exp in
+    rare halfway cases, so the bar is >= 99% agreement.  "ties" rows hold few
+    distinct values (sort order on equal logits: ascending index); "ragged"
+    rows have a vocabulary that is not a multiple of the sort's 1024-entry
+    rounds."""
     import oracle
     rng = np.random.default_rng(7)
-    M, n = 256, 16384
+    M, n = {"full": (256, 16384), "ties": (128, 16384), "ragged": (128, 5000)}[shape]
     lg = (rng.standard_normal((M, n)) * rng.choice([0.5, 2.0, 8.0], (M, 1))).astype(np.float32)
+    if shape == "ties":
+        lg = np.round(lg * 2.0).astype(np.float32) * np.float32(0.5)
+        lg[::4] = np.where(lg[::4] == 0.0, np.float32(-0.0), lg[::4])  # -0 and +0 compare equal
     u = rng.uniform(0, 1, M).astype(np.float32)
     cfg = {"top_p": (0.8, 0.95, 40, 0), "top_k": (0.8, 1.0, 40, 0), "temp": (0.8, 1.0, 0, 0)}[mode]
     sc = _lib.SamplingConfigC(*cfg)
@@ -203,4 +211,13 @@ def test_sampling_matches_oracle(olib, mode):
     got = out.cpu().numpy()
     oc = oracle.PfSamplingConfig(*cfg)
     want = np.array([olib.po_sample(np.ascontiguousarray(lg[i]), n, C.byref(oc), float(u[i])) for i in range(M)])
-    assert (got == want).mean() >= 0.99, (got != want).sum()
+    assert ((got >= 0) & (got < n)).all()
+    if shape == "ties" and mode != "temp":
+        # The reference's std::sort compares values only, so which of several
+        # equal logits sits at a sorted position is its implementation's
+        # choice; equal logits give equal terms and partial sums, so the draw
+        # lands on the same position and the same value.
+        rows = np.arange(M)
+        assert (lg[rows, got] == lg[rows, want]).mean() >= 0.99, (lg[rows, got] != lg[rows, want]).sum()
+    else:
+        assert (got == want).mean() >= 0.99, (got != want).sum()
