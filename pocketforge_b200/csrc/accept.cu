@@ -239,6 +239,153 @@ __device__ __forceinline__ void block_radix_sort(uint32_t (&k)[SORT_IPT], uint32
     }
 }
 
+constexpr int SORT_BUCKETS = 16384;  // value-range buckets: one per entry of the largest row
+constexpr int SORT_BUCKET_MAX = 64;   // larger buckets (many equal or clustered values): radix sort instead
+
+// Value-range bucket sort of the same items into the same order as
+// block_radix_sort.  bucket(v) = clamp((int)((hi - v) * (B / (hi - lo))), 0,
+// B-1) with [lo, hi] = mean -/+ 5 standard deviations of the row's finite
+// values: each float operation and the clamp are monotone, so the bucket
+// index never increases with v, the buckets in index order hold descending
+// values and equal values share a bucket, while outliers (a tied embedding's
+// own-token logit sits tens of deviations above the rest) collect in the end
+// buckets instead of stretching the range.  Within a bucket every entry counts
+// the entries that order before it (key, then index), all in parallel.  The
+// items in k / pv are consumed.  cnt holds SORT_BUCKETS counters, turned into
+// the buckets' starts in place.  Returns false, having written nothing the
+// radix sort reads, when the spread is not a positive finite number or a
+// bucket holds more than SORT_BUCKET_MAX entries; the result is uniform over
+// the CTA.
+__device__ __forceinline__ bool block_bucket_sort(uint32_t (&k)[SORT_IPT], uint32_t (&pv)[SORT_IPT], int R, int V,
+                                                  uint32_t* ks, uint32_t* vs, uint32_t* cnt, float* redf,
+                                                  uint32_t* wsum, uint32_t* wmax) {
+    constexpr int BPT = SORT_BUCKETS / SORT_THREADS;  // buckets per thread in the scan (16)
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    for (int i = tid; i < SORT_BUCKETS; i += SORT_THREADS) cnt[i] = 0;
+    float sx = 0.0f, sxx = 0.0f, nf = 0.0f;
+#pragma unroll
+    for (int r = 0; r < SORT_IPT; r++) {
+        if (r < R) {
+            const float v = key_value(k[r]);  // padding entries decode to NaN and are skipped
+            if (isfinite(v)) {
+                sx += v;
+                sxx = fmaf(v, v, sxx);
+                nf += 1.0f;
+            }
+        }
+    }
+    for (int o = 16; o >= 1; o >>= 1) {
+        sx += __shfl_xor_sync(0xffffffffu, sx, o);
+        sxx += __shfl_xor_sync(0xffffffffu, sxx, o);
+        nf += __shfl_xor_sync(0xffffffffu, nf, o);
+    }
+    if (lane == 0) {
+        redf[w] = sx;
+        redf[SORT_WARPS + w] = sxx;
+        redf[2 * SORT_WARPS + w] = nf;
+    }
+    __syncthreads();
+    sx = sxx = nf = 0.0f;
+    for (int i = 0; i < SORT_WARPS; i++) {
+        sx += redf[i];
+        sxx += redf[SORT_WARPS + i];
+        nf += redf[2 * SORT_WARPS + i];
+    }
+    const float mean = sx / nf, sd = sqrtf(fmaxf(sxx / nf - mean * mean, 0.0f));
+    const float hi = mean + 5.0f * sd, range = 10.0f * sd;
+    const float scale = __fdiv_rn((float)SORT_BUCKETS, range);
+    if (!(range > 0.0f && scale > 0.0f && isfinite(scale) && isfinite(hi))) return false;
+    auto bucket = [&](float v) {
+        return min(SORT_BUCKETS - 1, max(0, (int)__fmul_rn(__fsub_rn(hi, v), scale)));
+    };
+#pragma unroll
+    for (int r = 0; r < SORT_IPT; r++) {
+        if (r < R && w * 32 * R + r * 32 + lane < V)
+            pv[r] = (pv[r] & 0xffff0000u) | atomicAdd(&cnt[bucket(key_value(k[r]))], 1u);
+    }
+    __syncthreads();
+    // exclusive scan of the counts (thread t: buckets BPT*t ..) and the largest count
+    uint4* c4 = reinterpret_cast<uint4*>(cnt) + tid * (BPT / 4);
+    uint32_t s = 0, mc = 0;
+#pragma unroll
+    for (int q = 0; q < BPT / 4; q++) {
+        const uint4 c = c4[q];
+        s += c.x + c.y + c.z + c.w;
+        mc = max(mc, max(max(c.x, c.y), max(c.z, c.w)));
+    }
+    uint32_t incl = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+        mc = max(mc, __shfl_xor_sync(0xffffffffu, mc, o));
+    }
+    if (lane == 31) wsum[w] = incl;
+    if (lane == 0) wmax[w] = mc;
+    __syncthreads();
+    uint32_t run = incl - s;
+    for (int i = 0; i < SORT_WARPS; i++) {
+        if (i < w) run += wsum[i];
+        mc = max(mc, wmax[i]);
+    }
+    if (mc > (uint32_t)SORT_BUCKET_MAX) return false;
+#pragma unroll
+    for (int q = 0; q < BPT / 4; q++) {  // this thread's own counters, read again and replaced by starts
+        const uint4 c = c4[q];
+        uint4 o;
+        o.x = run;
+        run += c.x;
+        o.y = run;
+        run += c.y;
+        o.z = run;
+        run += c.z;
+        o.w = run;
+        run += c.w;
+        c4[q] = o;
+    }
+    __syncthreads();
+    const uint32_t* start = cnt;
+#pragma unroll
+    for (int r = 0; r < SORT_IPT; r++) {
+        const int j = w * 32 * R + r * 32 + lane;
+        if (r < R && j < V) {
+            const uint32_t pos = start[bucket(key_value(k[r]))] + (pv[r] & 0xffffu);
+            ks[pos] = k[r];
+            vs[pos] = (uint32_t)j;
+        }
+    }
+    __syncthreads();
+    // Order within the buckets: the entry at position i moves to its bucket's
+    // start + the number of the bucket's entries ordered before it (key, then
+    // index: a permutation, the indices being distinct).  Ranks are taken for
+    // all positions before any entry moves.
+#pragma unroll
+    for (int r = 0; r < SORT_IPT; r++) {
+        const int i = tid + r * SORT_THREADS;
+        if (r < R && i < V) {
+            const uint32_t kk = ks[i], vv = vs[i];
+            const int bk = bucket(key_value(kk));
+            const int s0 = (int)start[bk], e = bk + 1 < SORT_BUCKETS ? (int)start[bk + 1] : V;
+            const unsigned long long me = ((unsigned long long)kk << 32) | vv;
+            int rank = 0;
+            for (int j = s0; j < e; j++) rank += (((unsigned long long)ks[j] << 32) | vs[j]) < me;
+            k[r] = kk;
+            pv[r] = ((uint32_t)(s0 + rank) << 16) | vv;
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < SORT_IPT; r++) {
+        const int i = tid + r * SORT_THREADS;
+        if (r < R && i < V) {
+            ks[pv[r] >> 16] = k[r];
+            vs[pv[r] >> 16] = pv[r] & 0xffffu;
+        }
+    }
+    __syncthreads();
+    return true;
+}
+
 // One thread's cumulative float sum of a[0, n) in index order, continuing
 // from cum.  Returns the first i whose partial sum c satisfies stop(c) (cum is
 // then that sum), else n (cum is the full sum).  The terms are >= 0, so the
@@ -302,8 +449,8 @@ __global__ void __launch_bounds__(SORT_THREADS, 1)
     uint32_t* vs = ks + cap;
     uint32_t* hist = vs + cap;
     float* key = reinterpret_cast<float*>(sm);  // values / terms, in place of ks
-    __shared__ float red[SORT_WARPS];
-    __shared__ uint32_t wsum[SORT_WARPS];
+    __shared__ float red[3 * SORT_WARPS];
+    __shared__ uint32_t wsum[SORT_WARPS], wmax[SORT_WARPS];
     const int b = blockIdx.x;
     if (b >= n) return;
     const float* lg = logits + (size_t)rows[b] * ld;
@@ -354,7 +501,8 @@ __global__ void __launch_bounds__(SORT_THREADS, 1)
                 pv[r] = (uint32_t)(j < V ? j : 0xffff) << 16;
             }
         }
-        block_radix_sort(k, pv, R, ks, vs, hist, wsum);
+        if (!block_bucket_sort(k, pv, R, V, ks, vs, hist, red, wsum, wmax))
+            block_radix_sort(k, pv, R, ks, vs, hist, wsum);
     }
     const float mx = key_value(ks[0]);
     const int nn = top_p ? V : (int)cfg.top_k;
@@ -393,12 +541,14 @@ pf_status sample_rows(const float* logits, int ld, int V, const int* rows, int n
                       const float* uniforms, int ustride, int* out, cudaStream_t st) {
     PF_CHECK(V >= 1 && V <= SORT_THREADS * SORT_IPT, "sample_rows: vocabulary above 16384 is not supported");
     const int R = (V + SORT_THREADS - 1) / SORT_THREADS;
-    const size_t smem = (size_t)R * SORT_THREADS * 2 * sizeof(uint32_t) + SORT_WARPS * SORT_RADIX * sizeof(uint32_t);
+    // keys + indices, then the bucket counters (the radix histogram shares their space)
+    constexpr size_t kCounters = SORT_BUCKETS * sizeof(uint32_t);
+    static_assert(SORT_WARPS * SORT_RADIX * sizeof(uint32_t) <= kCounters, "histogram fits the counters");
+    const size_t smem = (size_t)R * SORT_THREADS * 2 * sizeof(uint32_t) + kCounters;
     static bool attr = false;
     if (!attr) {
         PF_CUDA(cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     SORT_THREADS * SORT_IPT * 2 * sizeof(uint32_t) +
-                                         SORT_WARPS * SORT_RADIX * sizeof(uint32_t)));
+                                     SORT_THREADS * SORT_IPT * 2 * sizeof(uint32_t) + kCounters));
         attr = true;
     }
     sample_kernel<<<n, SORT_THREADS, smem, st>>>(logits, ld, V, R, rows, n, cfg, uniforms, ustride, out);

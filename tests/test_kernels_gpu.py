@@ -193,9 +193,10 @@ def test_sampling_matches_oracle(olib, mode, shape):
     are the reference's float sums in its order; the exponentials are double
     exp rounded to float, which can differ from the C library's float exp in
     rare halfway cases, so the bar is >= 99% agreement.  "ties" rows hold few
-    distinct values (sort order on equal logits: ascending index); "ragged"
-    rows have a vocabulary that is not a multiple of the sort's 1024-entry
-    rounds."""
+    distinct values (sort order on equal logits: ascending index; the value
+    buckets overflow, so the radix sort runs); "ragged" rows have a vocabulary
+    that is not a multiple of the sort's 1024-entry rounds and ten masked
+    (-inf) entries; "full" and "ragged" rows take the bucket sort."""
     import oracle
     rng = np.random.default_rng(7)
     M, n = {"full": (256, 16384), "ties": (128, 16384), "ragged": (128, 5000)}[shape]
@@ -203,6 +204,8 @@ def test_sampling_matches_oracle(olib, mode, shape):
     if shape == "ties":
         lg = np.round(lg * 2.0).astype(np.float32) * np.float32(0.5)
         lg[::4] = np.where(lg[::4] == 0.0, np.float32(-0.0), lg[::4])  # -0 and +0 compare equal
+    if shape == "ragged":
+        lg[:, rng.choice(n, 10, replace=False)] = -np.inf  # masked entries: zero terms
     u = rng.uniform(0, 1, M).astype(np.float32)
     cfg = {"top_p": (0.8, 0.95, 40, 0), "top_k": (0.8, 1.0, 40, 0), "temp": (0.8, 1.0, 0, 0)}[mode]
     sc = _lib.SamplingConfigC(*cfg)
