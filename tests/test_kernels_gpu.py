@@ -186,7 +186,7 @@ def test_argmax_first_max(olib):
     assert got[3] == 10 and got[4] == 0 and got[5] == n - 1
 
 
-@pytest.mark.parametrize("shape", ["full", "ties", "ragged"])
+@pytest.mark.parametrize("shape", ["full", "ties", "ragged", "outlier", "flat"])
 @pytest.mark.parametrize("mode", ["top_p", "top_k", "temp"])
 def test_sampling_matches_oracle(olib, mode, shape):
     """Same logits and uniform draws: the sampled token must agree.  The sums
@@ -196,16 +196,24 @@ def test_sampling_matches_oracle(olib, mode, shape):
     distinct values (sort order on equal logits: ascending index; the value
     buckets overflow, so the radix sort runs); "ragged" rows have a vocabulary
     that is not a multiple of the sort's 1024-entry rounds and ten masked
-    (-inf) entries; "full" and "ragged" rows take the bucket sort."""
+    (-inf) entries; "outlier" rows carry one logit 45 deviations above the rest
+    (a tied embedding's own-token logit: it lands in an end bucket); "full",
+    "ragged" and "outlier" rows take the bucket sort, "flat" rows (half the
+    entries one value) overflow a bucket and take the radix sort."""
     import oracle
     rng = np.random.default_rng(7)
-    M, n = {"full": (256, 16384), "ties": (128, 16384), "ragged": (128, 5000)}[shape]
+    M, n = {"full": (256, 16384), "ties": (128, 16384), "ragged": (128, 5000), "outlier": (128, 16384),
+            "flat": (64, 16384)}[shape]
     lg = (rng.standard_normal((M, n)) * rng.choice([0.5, 2.0, 8.0], (M, 1))).astype(np.float32)
     if shape == "ties":
         lg = np.round(lg * 2.0).astype(np.float32) * np.float32(0.5)
         lg[::4] = np.where(lg[::4] == 0.0, np.float32(-0.0), lg[::4])  # -0 and +0 compare equal
     if shape == "ragged":
         lg[:, rng.choice(n, 10, replace=False)] = -np.inf  # masked entries: zero terms
+    if shape == "outlier":
+        lg[np.arange(M), rng.integers(0, n, M)] = 45.0 * lg.std(axis=1)
+    if shape == "flat":
+        lg[:, rng.choice(n, n // 2, replace=False)] = np.float32(-1.0)
     u = rng.uniform(0, 1, M).astype(np.float32)
     cfg = {"top_p": (0.8, 0.95, 40, 0), "top_k": (0.8, 1.0, 40, 0), "temp": (0.8, 1.0, 0, 0)}[mode]
     sc = _lib.SamplingConfigC(*cfg)
@@ -215,7 +223,7 @@ def test_sampling_matches_oracle(olib, mode, shape):
     oc = oracle.PfSamplingConfig(*cfg)
     want = np.array([olib.po_sample(np.ascontiguousarray(lg[i]), n, C.byref(oc), float(u[i])) for i in range(M)])
     assert ((got >= 0) & (got < n)).all()
-    if shape == "ties" and mode != "temp":
+    if shape in ("ties", "flat") and mode != "temp":
         # The reference's std::sort compares values only, so which of several
         # equal logits sits at a sorted position is its implementation's
         # choice; equal logits give equal terms and partial sums, so the draw
