@@ -545,12 +545,8 @@ pf_status sample_rows(const float* logits, int ld, int V, const int* rows, int n
     constexpr size_t kCounters = SORT_BUCKETS * sizeof(uint32_t);
     static_assert(SORT_WARPS * SORT_RADIX * sizeof(uint32_t) <= kCounters, "histogram fits the counters");
     const size_t smem = (size_t)R * SORT_THREADS * 2 * sizeof(uint32_t) + kCounters;
-    static bool attr = false;
-    if (!attr) {
-        PF_CUDA(cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     SORT_THREADS * SORT_IPT * 2 * sizeof(uint32_t) + kCounters));
-        attr = true;
-    }
+    static std::atomic<uint64_t> attr{0};
+    PF_TRY(raise_smem_limit(sample_kernel, SORT_THREADS * SORT_IPT * 2 * sizeof(uint32_t) + kCounters, attr));
     sample_kernel<<<n, SORT_THREADS, smem, st>>>(logits, ld, V, R, rows, n, cfg, uniforms, ustride, out);
     return launch_check("sample_rows");
 }

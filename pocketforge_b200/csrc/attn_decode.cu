@@ -766,11 +766,8 @@ static pf_status launch_decode(const KvCache& kv, int layer, const RowBatch& rb,
                                int v_col, int H, Staged st, SpecPool sp, const AttnWork& aw, float* out, int ldo,
                                cudaStream_t stream) {
     const int smem = (int)sizeof(AttnSmem<MT, NEX>);
-    static bool attr = false;
-    if (!attr) {
-        PF_CUDA(cudaFuncSetAttribute(attn_decode_kernel<MT, NEX>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        attr = true;
-    }
+    static std::atomic<uint64_t> attr{0};
+    PF_TRY(raise_smem_limit(attn_decode_kernel<MT, NEX>, smem, attr));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(rb.nb, kv.G, aw.nsplit * attention_decode_row_groups(kv, H, rb.max_rows));
     cfg.blockDim = dim3(128);

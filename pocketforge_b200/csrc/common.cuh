@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <cstdio>
 #include <string>
 
@@ -54,6 +55,20 @@ enum : uint32_t {
     ERR_CONTEXT = 8u      // a position beyond the cache capacity
 };
 uint32_t* device_error_flag();  // per-device global (allocated on first use)
+
+// cudaFuncSetAttribute acts on the current device's instance of a kernel, so the
+// raised dynamic shared-memory limit is recorded per device: `done` holds one bit
+// per device id (< 64; above that the attribute is set on every call).
+template <typename Kernel>
+inline pf_status raise_smem_limit(Kernel kernel, size_t bytes, std::atomic<uint64_t>& done) {
+    int dev = 0;
+    PF_CUDA(cudaGetDevice(&dev));
+    const uint64_t bit = dev < 64 ? (1ull << dev) : 0ull;
+    if (bit && (done.load(std::memory_order_acquire) & bit)) return PF_OK;
+    PF_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+    done.fetch_or(bit, std::memory_order_acq_rel);
+    return PF_OK;
+}
 
 __host__ __device__ inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
 

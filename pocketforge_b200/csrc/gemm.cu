@@ -296,12 +296,8 @@ __global__ void __launch_bounds__(NT) gemm_kernel(const GemmParams p) {
 template <int NPL, int WF, int EPI>
 pf_status launch_t(const GemmParams& p, cudaStream_t st) {
     const int smem = 2 * NPL * BM * A_STRIDE;
-    static bool attr_set = false;
-    if (!attr_set) {
-        PF_CUDA(cudaFuncSetAttribute(gemm_kernel<NPL, WF, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     smem));
-        attr_set = true;
-    }
+    static std::atomic<uint64_t> attr{0};
+    PF_TRY(raise_smem_limit(gemm_kernel<NPL, WF, EPI>, smem, attr));
     dim3 grid(p.N / BN, ceil_div(p.M, BM), p.splits);
     gemm_kernel<NPL, WF, EPI><<<grid, NT, smem, st>>>(p);
     return launch_check("gemm");

@@ -601,12 +601,8 @@ pf_status launch_tc(const GemmParams& p, int plane_rows, cudaStream_t st) {
     PF_TRY(make_map(&ta, p.A, (uint64_t)p.K, a_rows, (uint64_t)p.lda, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B));
     PF_TRY(make_map(&tb, p.W, (uint64_t)row_bytes<WF>(), (uint64_t)(p.K / BK) * p.N, (uint64_t)row_bytes<WF>(),
                     row_bytes<WF>(), BN, CU_TENSOR_MAP_SWIZZLE_NONE));
-    static bool attr = false;
-    if (!attr) {
-        PF_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, P, WF, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     Ly::SMEM));
-        attr = true;
-    }
+    static std::atomic<uint64_t> attr{0};
+    PF_TRY(raise_smem_limit(gemm_tc_kernel<BN, P, WF, EPI>, Ly::SMEM, attr));
     dim3 grid(p.N / BN, ceil_div(p.M, BM), p.splits);
     uint32_t* err = device_error_flag();
     if (p.pdl) {
