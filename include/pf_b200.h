@@ -123,13 +123,14 @@ PF_API pf_status pf_dequant_ternary_to_int8(const uint8_t* src, int8_t* dst,
                                      int64_t n, void* stream);
 
 /* forge::matmul_int8 (include/forge/matmul_neon.hpp:55-62):
- * C[M][N] (int32) = A[M][K] (int8) . B[N][K]^T (int8). */
+ * C[M][N] (int32) = A[M][K] (int8) . B[N][K]^T (int8).  M = 0 does nothing. */
 PF_API pf_status pf_matmul_int8(const int8_t* A, const int8_t* B, int32_t* C,
                          int32_t M, int32_t N, int32_t K, void* stream);
 
 /* forge::matmul_quantized (include/forge/matmul_neon.hpp:68-77):
  * C = ((float)(quant(A) . B^T) * a_scale[i]) * w_scale[j].
- * act_scales may be NULL (computed per row, as the engine always does). */
+ * act_scales may be NULL (computed per row, as the engine always does).
+ * M = 0 does nothing. */
 PF_API pf_status pf_matmul_quantized(const float* A, const int8_t* B, float* C,
                               int32_t M, int32_t N, int32_t K,
                               const float* weight_scales, const float* act_scales,
@@ -217,7 +218,8 @@ PF_API pf_status pf_pack_weights(const int8_t* w, int32_t rows, int32_t cols,
 
 /* The projection kernel of the engine: C = (int32)(Aq . unpack(W)^T) with the
  * scale epilogue of matmul_quantized (src/matmul_neon.cpp:176-180):
- * C[i][j] = ((float)acc * a_scale[i]) * w_scale[j]. Aq int8 [M][K]. */
+ * C[i][j] = ((float)acc * a_scale[i]) * w_scale[j]. Aq int8 [M][K].
+ * M = 0 does nothing. */
 PF_API pf_status pf_gemm_packed(const int8_t* Aq, const float* a_scale,
                          const void* packed_w, const float* w_scale, int32_t qtype,
                          float* C, int32_t M, int32_t N, int32_t K, void* stream);

@@ -73,12 +73,16 @@ pf_status pf_dequant_ternary_to_int8(const uint8_t* src, int8_t* dst, int64_t n,
 pf_status pf_pack_weights(const int8_t* w, int32_t rows, int32_t cols, int32_t qtype, void* packed, void* stream) {
     PF_TRY(require_device());
     PF_CHECK(qtype >= 0 && qtype <= 3, "pf_pack_weights: bad qtype %d", qtype);
+    PF_CHECK(rows >= 0 && cols > 0, "pf_pack_weights: bad shape %d x %d", rows, cols);
+    if (rows == 0) return PF_OK;  // no rows: nothing to pack
     return pack_weights_tc(w, rows, cols, wfmt_of_qtype(qtype), packed, as_stream(stream));
 }
 
 pf_status pf_gemm_packed(const int8_t* Aq, const float* a_scale, const void* packed_w, const float* w_scale,
                          int32_t qtype, float* C, int32_t M, int32_t N, int32_t K, void* stream) {
     PF_TRY(require_device());
+    PF_CHECK(M >= 0, "pf_gemm_packed: M=%d", M);
+    if (M == 0) return PF_OK;  // no rows: nothing to compute (as the reference's row loop)
     PF_CHECK(Aq && a_scale && packed_w && C, "pf_gemm_packed: null argument");
     GemmParams p;
     p.A = Aq; p.lda = K; p.a_scale = a_scale; p.M = M; p.N = N; p.K = K;
@@ -90,7 +94,9 @@ pf_status pf_gemm_packed(const int8_t* Aq, const float* a_scale, const void* pac
 pf_status pf_matmul_int8(const int8_t* A, const int8_t* B, int32_t* C, int32_t M, int32_t N, int32_t K,
                          void* stream) {
     PF_TRY(require_device());
-    PF_CHECK(A && B && C && M > 0 && N > 0 && K > 0, "pf_matmul_int8: bad arguments");
+    PF_CHECK(M >= 0 && N > 0 && K > 0, "pf_matmul_int8: bad shape");
+    if (M == 0) return PF_OK;  // no rows: nothing to compute (as the reference's row loop)
+    PF_CHECK(A && B && C, "pf_matmul_int8: null argument");
     cudaStream_t st = as_stream(stream);
     const int Kp = round_up(K, 128), Np = round_up(N, 64);
     Scratch s(st);
@@ -116,7 +122,9 @@ pf_status pf_matmul_int8(const int8_t* A, const int8_t* B, int32_t* C, int32_t M
 pf_status pf_matmul_quantized(const float* A, const int8_t* B, float* C, int32_t M, int32_t N, int32_t K,
                               const float* weight_scales, const float* act_scales, void* stream) {
     PF_TRY(require_device());
-    PF_CHECK(A && B && C && weight_scales && M > 0 && N > 0 && K > 0, "pf_matmul_quantized: bad arguments");
+    PF_CHECK(M >= 0 && N > 0 && K > 0, "pf_matmul_quantized: bad shape");
+    if (M == 0) return PF_OK;  // no rows: nothing to compute (as the reference's row loop)
+    PF_CHECK(A && B && C && weight_scales, "pf_matmul_quantized: null argument");
     cudaStream_t st = as_stream(stream);
     const int Kp = round_up(K, 128), Np = round_up(N, 64);
     Scratch s(st);

@@ -232,3 +232,33 @@ def test_sampling_matches_oracle(olib, mode, shape):
         assert (lg[rows, got] == lg[rows, want]).mean() >= 0.99, (lg[rows, got] != lg[rows, want]).sum()
     else:
         assert (got == want).mean() >= 0.99, (got != want).sum()
+
+
+def test_empty_batches_are_noops():
+    """Zero rows (or zero bytes) do nothing and return PF_OK, as the reference's
+    row loops do; a bad shape is refused on the host (PF_ERR_INVALID) before
+    any launch."""
+    L = _lib.lib()
+    f = torch.zeros(256, device="cuda")
+    i8 = torch.zeros(256 * 128, dtype=torch.int8, device="cuda")
+    i32 = torch.zeros(256, dtype=torch.int32, device="cuda")
+    packed = torch.zeros(L.pf_packed_weight_bytes(64, 128, 1), dtype=torch.uint8, device="cuda")
+    sc = _lib.SamplingConfigC(0.8, 0.95, 40, 0)
+    calls = {
+        "pf_quantize_activation_rows": (p(f), p(i8), p(f), 0, 128, None),
+        "pf_dequant_q4_to_int8": (p(i8), p(i8), C.c_float(1.0), 0, None),
+        "pf_dequant_ternary_to_int8": (p(i8), p(i8), 0, None),
+        "pf_matmul_int8": (p(i8), p(i8), p(i32), 0, 64, 128, None),
+        "pf_matmul_quantized": (p(f), p(i8), p(f), 0, 64, 128, p(f), None, None),
+        "pf_gemm_packed": (p(i8), p(f), p(packed), p(f), 1, p(f), 0, 64, 128, None),
+        "pf_pack_weights": (p(i8), 0, 128, 1, p(packed), None),
+        "pf_rmsnorm_rows": (p(f), p(f), p(f), 0, 128, None),
+        "pf_softmax_rows": (p(f), 0, 128, None),
+        "pf_argmax_rows": (p(f), 0, 128, p(i32), None),
+        "pf_sample_rows": (p(f), 0, 128, C.byref(sc), p(f), p(i32), None),
+    }
+    for name, args in calls.items():
+        assert getattr(L, name)(*args) == 0, (name, L.pf_last_error())
+    torch.cuda.synchronize()
+    assert L.pf_matmul_int8(p(i8), p(i8), p(i32), 4, 0, 128, None) == 1  # N = 0: PF_ERR_INVALID
+    assert L.pf_gemm_packed(p(i8), p(f), p(packed), p(f), 1, p(f), 4, 64, 100, None) == 1  # K % 128 != 0
