@@ -393,7 +393,17 @@ __device__ __forceinline__ bool block_bucket_sort(uint32_t (&k)[SORT_IPT], uint3
 // terms; only the group that holds the stop is added again, term by term.
 // The next 16 terms are loaded before the current 16 are added (a is 16-byte
 // aligned), so the loop runs at the latency of the dependent additions.
-template <typename Stop>
+// DESC: the terms never increase (sorted rows).  Then once a term is below a
+// quarter of the spacing of floats above the sum, every later term rounds
+// away (RN(c + q) = c for 0 <= q < ulp(c)/2; the factor 2 of margin covers a
+// term one float step above its predecessor, the double exp being within an
+// ulp but not guaranteed monotone): the sum is final and a stop that has not
+// held cannot start to, so the scan ends with the result of the full walk.
+__device__ __forceinline__ float quarter_ulp(float c) {  // c >= 0; 0 when too small to matter
+    const uint32_t e = __float_as_uint(c) >> 23;
+    return e >= 26 ? __uint_as_float((e - 25) << 23) : 0.0f;
+}
+template <bool DESC, typename Stop>
 __device__ __forceinline__ int ordered_scan(const float* a, int n, float& cum, Stop stop) {
     const int n16 = n & ~15;
     const float4* a4 = reinterpret_cast<const float4*>(a);
@@ -429,6 +439,10 @@ __device__ __forceinline__ int ordered_scan(const float* a, int n, float& cum, S
                     return i + j;
                 }
             }
+        }
+        if (DESC && t3.w < quarter_ulp(c)) {
+            cum = c;
+            return n;
         }
     }
     cum = c;
@@ -476,7 +490,7 @@ __global__ void __launch_bounds__(SORT_THREADS, 1)
         __syncthreads();
         if (tid == 0) {
             float sum = 0.0f;
-            ordered_scan(key, V, sum, [](float) { return false; });
+            ordered_scan<false>(key, V, sum, [](float) { return false; });
             red[1] = sum;
         }
         __syncthreads();
@@ -485,7 +499,7 @@ __global__ void __launch_bounds__(SORT_THREADS, 1)
         __syncthreads();
         if (tid == 0) {
             float cum = 0.0f;
-            const int i = ordered_scan(key, V, cum, [u](float c) { return u <= c; });
+            const int i = ordered_scan<false>(key, V, cum, [u](float c) { return u <= c; });
             out[b] = i < V ? i : V - 1;
         }
         return;
@@ -513,7 +527,7 @@ __global__ void __launch_bounds__(SORT_THREADS, 1)
     if (tid == 0) {
         // terms after the first zero are zero too (sorted descending) and add nothing
         float total = 0.0f;
-        ordered_scan(key, nn, total, [](float) { return false; });
+        ordered_scan<true>(key, nn, total, [](float) { return false; });
         red[0] = total;
     }
     __syncthreads();
@@ -530,9 +544,9 @@ __global__ void __launch_bounds__(SORT_THREADS, 1)
         // entry by then takes the last kept one, entry i.  Either way the
         // token is the entry where the first of the two holds.
         const float p = cfg.top_p;
-        i = ordered_scan(key, nn, cum, [u, p](float c) { return u <= c || c >= p; });
+        i = ordered_scan<true>(key, nn, cum, [u, p](float c) { return u <= c || c >= p; });
     } else {  // top-k (src/engine.cpp:930-959)
-        i = ordered_scan(key, nn, cum, [u](float c) { return u <= c; });
+        i = ordered_scan<true>(key, nn, cum, [u](float c) { return u <= c; });
     }
     out[b] = (int)vs[i < nn ? i : nn - 1];
 }
