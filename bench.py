@@ -33,6 +33,28 @@ sys.path.insert(0, ROOT)
 
 METRIC = "accepted tok/s"
 UNIT = "tok/s"
+MTP_PROBE_STEPS = 4  # untimed steps after the timed region that record per-head acceptance
+
+
+def measure_int8_peak():
+    """int8 tensor-core peak of this GPU, measured: the best of 10 cuBLASLt
+    int8 GEMMs (torch._int_mm) of 8192^3, 2*8192^3 operations each."""
+    import torch
+    n = 8192
+    a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda")
+    b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda").t()
+    best = float("inf")
+    for i in range(13):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch._int_mm(a, b)
+        e1.record()
+        e1.synchronize()
+        if i >= 3:
+            best = min(best, e0.elapsed_time(e1))
+    del a, b
+    torch.cuda.empty_cache()
+    return 2 * n ** 3 / (best * 1e-3) / 1e12
 
 
 def load_peaks():
@@ -239,7 +261,8 @@ def main():
     plen = args.prompt or preset["prompt"]
     K = model.n_mtp_heads
     R = K + 1
-    max_pos = plen + (args.warmup + args.steps + 2) * R + 8
+    # room for: warm-up, timed steps, 2 kernel-timing steps, MTP_PROBE_STEPS
+    max_pos = plen + (args.warmup + args.steps + 2 + MTP_PROBE_STEPS) * R + 8
     if model.max_context < max_pos:
         max_pos = model.max_context
     eng = pf.BatchEngine(model, seqs, max_pos, device=local)
@@ -305,6 +328,37 @@ def main():
     eng.run_steps(2)
     (attn_ms, attn_n), (proj_ms, proj_n) = eng.kernel_times()
     eng.set_kernel_timing(False)
+    # ---- MTP drafts on this synthetic model (untimed): the fraction of each
+    # head's logit rows that are finite (the chained heads can overflow float
+    # range, in the reference's arithmetic as well) and how often each draft
+    # position is accepted.
+    mtp_rows = eng.read_mtp_logits()
+    mtp_finite = np.isfinite(mtp_rows).all(axis=-1).mean(axis=0)
+    del mtp_rows
+    accepted_at = np.zeros(K)
+    for _ in range(MTP_PROBE_STEPS):
+        n_em, _ = eng.step()
+        accepted_at += [(n_em - 1 > h).mean() for h in range(K)]
+    accepted_at /= MTP_PROBE_STEPS
+    # ---- strong scaling beside weak (N > 1): the config's own batch split
+    # over the ranks, on the same engines, same steps.
+    strong = None
+    if world > 1 and not args.strong:
+        s0, s1 = replicas.sequence_slice(args.seqs or preset["seqs"], world, rank)
+        sprompts = make_prompts(range(s0, s1), plen, model.n_vocab)
+        sseeds = [sampling["seed"] + i for i in range(s0, s1)] if sampling else None
+        eng.prefill(sprompts, sseeds)
+        eng.run_steps(args.warmup)
+        spos0 = eng.read_positions().astype(np.int64)
+        dist.barrier()
+        torch.cuda.synchronize()
+        sms = eng.run_steps(args.steps)
+        torch.cuda.synchronize()
+        stok = int((eng.read_positions().astype(np.int64) - spos0).sum())
+        sms_max, stok_all = replicas.step_totals(sms, stok)
+        strong = {"value": stok_all / (sms_max * 1e-3), "unit": UNIT, "global_seqs": args.seqs or preset["seqs"],
+                  "seqs_per_gpu": s1 - s0, "ms_per_step": sms_max / args.steps, "scaling": "strong"}
+    int8_peak = measure_int8_peak() if rank == 0 else None
     ms_max, tokens_all = replicas.step_totals(ms, tokens)
     per_rank = replicas.gather_to_root({"rank": rank, "device_ms": ms, "tokens": tokens})
     step_ms = ms / args.steps
@@ -357,8 +411,15 @@ def main():
                                          "algorithmic_bytes": proj_bytes,
                                          "achieved_gbs": proj_bytes / (proj_ms * 1e-3) / 1e9,
                                          "int8_tops": proj_ops / (proj_ms * 1e-3) / 1e12,
-                                         "int8_peak_tops": 4500.0,
-                                         "int8_peak_kind": "nominal dense int8 (2 x the 2.25 PF dense bf16)"}},
+                                         "int8_peak_tops": int8_peak,
+                                         "int8_frac": proj_ops / (proj_ms * 1e-3) / 1e12 / int8_peak,
+                                         "int8_peak_kind": "measured: best of 10 torch._int_mm 8192^3 on this GPU"}},
+            "mtp": {"finite_frac_per_head": [round(float(x), 4) for x in mtp_finite],
+                    "mtp_finite_frac": float(mtp_finite.mean()),
+                    "accepted_frac_per_draft": [round(float(x), 4) for x in accepted_at],
+                    "note": "synthetic heads (reference MTPHeads::quantize_q4 of seeded uniform weights) chained "
+                            "h += down(silu(gate h) * up h); rows whose logits overflow float range give "
+                            "arbitrary drafts, in the reference's arithmetic as well"},
             "cpu_baseline": cpu,
             "e2e": e2e,
             "clocks": clocks,
@@ -366,6 +427,12 @@ def main():
         }
         if world > 1:
             line["per_rank"] = per_rank
+        if strong is not None:
+            line["extra"] = {"strong": strong}
+        if model.skip_enabled:
+            comp, skp = eng.read_skip_counts()
+            line["layer_skip"] = {"threshold": model.skip_threshold, "ffn_computed": comp, "ffn_skipped": skp,
+                                  "skipped_frac": skp / max(1, comp + skp)}
         print(json.dumps(line))
     eng.close()
     if world > 1:

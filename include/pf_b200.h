@@ -229,11 +229,12 @@ PF_API pf_status pf_gemm_packed(const int8_t* Aq, const float* a_scale,
  * library (no counterpart in the reference, which has no device memory).
  * For callers that cannot call cudaMalloc — a runtime whose own pool owns all
  * device memory, or a path that must not risk the device synchronisation an
- * allocation can cause.  Limits: M*N <= 1,048,576 and ceil(M/64)*(N/64) <=
- * 4096 (else PF_ERR_INVALID).  Every GPU that loads the library holds the
- * 4 MiB array until exit; calls share it, so calls that overlap on the GPU
- * race.  The first call on a device sets the array up synchronously: make it
- * before any stream capture. */
+ * allocation can cause.  Limits: M*N <= 1,048,576 and ceil(M/128)*ceil(N/64)
+ * <= 4096 (else PF_ERR_INVALID); M = 0 does nothing.  Every GPU that loads
+ * the library holds the 4 MiB array until exit; calls share it, so calls that
+ * overlap on the GPU race.  The first call on a device loads the array's
+ * module there: make it before any stream capture.  The array's address is
+ * looked up on every call, so calls stay valid after cudaDeviceReset. */
 PF_API pf_status pf_gemm_packed_static(const int8_t* Aq, const float* a_scale, const void* packed_w,
                                        const float* w_scale, int32_t qtype, float* C, int32_t M, int32_t N,
                                        int32_t K, void* stream);

@@ -762,7 +762,30 @@ struct Seq {
     std::vector<int32_t> drafts;
     std::mt19937 rng;
     std::vector<float> mtp_logits;  // [K][V] of the last MTP call
+    // Committed FFN decisions of this sequence, and the smallest layer-skip
+    // decision margin seen (a test diagnostic).  Kept per sequence so that
+    // sequences can run on separate host threads; the engine sums them.
+    int64_t ffn_computed = 0, ffn_skipped = 0;
+    float skip_margin = INFINITY;
 };
+
+// Runs f(0..n-1) on up to `threads` host threads.  Each index is one
+// sequence: sequences share no mutable state, so the results are the same
+// as running them one after another.
+template <class F>
+static void for_each_seq(int n, int threads, F f) {
+    if (threads <= 1 || n <= 1) {
+        for (int i = 0; i < n; i++) f(i);
+        return;
+    }
+    std::atomic<int> next{0};
+    std::vector<std::thread> pool;
+    for (int t = 0; t < std::min(threads, n); t++)
+        pool.emplace_back([&]() {
+            for (int i; (i = next++) < n;) f(i);
+        });
+    for (auto& th : pool) th.join();
+}
 
 struct Engine {
     pf_model_config cfg{};
@@ -774,8 +797,23 @@ struct Engine {
     std::vector<MtpHead> mtp;
     std::vector<Seq> seqs;
     std::vector<float> last_logits;  // [n_seqs*(K+1)][V]
-    int64_t ffn_computed = 0, ffn_skipped = 0;
-    float skip_margin = INFINITY;  // smallest decision margin seen (test diagnostic)
+    int threads = 1;                 // host threads over sequences (prefill, step)
+
+    int64_t ffn_computed() const {
+        int64_t n = 0;
+        for (const Seq& s : seqs) n += s.ffn_computed;
+        return n;
+    }
+    int64_t ffn_skipped() const {
+        int64_t n = 0;
+        for (const Seq& s : seqs) n += s.ffn_skipped;
+        return n;
+    }
+    float skip_margin() const {  // smallest decision margin seen (test diagnostic)
+        float m = INFINITY;
+        for (const Seq& s : seqs) m = std::min(m, s.skip_margin);
+        return m;
+    }
 
     uint32_t d() const { return (uint32_t)cfg.n_embd; }
     uint32_t K() const { return (uint32_t)cfg.n_mtp_heads; }
@@ -875,12 +913,12 @@ struct Engine {
             rmsnorm(nrm.data(), x.data(), ffn_norm.data() + (size_t)l * D, D, cfg.norm_eps, order);
             float mg = INFINITY;
             const bool skip = cfg.skip_enabled ? s.skip.should_skip(l, nrm.data(), order, &mg) : false;
-            skip_margin = std::min(skip_margin, mg);
+            s.skip_margin = std::min(s.skip_margin, mg);
             if (skip) {
-                ffn_skipped++;
+                s.ffn_skipped++;
                 continue;
             }
-            ffn_computed++;
+            s.ffn_computed++;
             mm_quant(nrm.data(), w[PF_MAT_GATE][l].data(), g.data(), 1, F, D, rs[PF_MAT_GATE][l].data(), nullptr);
             mm_quant(nrm.data(), w[PF_MAT_UP][l].data(), u.data(), 1, F, D, rs[PF_MAT_UP][l].data(), nullptr);
             for (uint32_t j = 0; j < F; j++) act[j] = swiglu_engine(g[j], u[j]);
@@ -913,8 +951,8 @@ struct Engine {
         seqs.clear();
         seqs.resize(n);
         const bool greedy = sampling_is_greedy(samp);
-        std::vector<float> lg(V());
-        for (int32_t b = 0; b < n; b++) {
+        for_each_seq(n, threads, [&](int b) {
+            std::vector<float> lg(V());
             Seq& s = seqs[b];
             new_seq(s, seeds ? seeds[b] : 0u);
             const int64_t a = off[b], e = off[b + 1];
@@ -925,7 +963,7 @@ struct Engine {
             }
             s.pending = greedy ? argmax(lg.data(), V()) : sample(lg.data(), V(), samp, draw(s));
             draft(s);
-        }
+        });
         last_logits.assign((size_t)n * (K() + 1) * V(), 0.0f);
     }
 
@@ -933,16 +971,16 @@ struct Engine {
     void step(int32_t* n_emitted, int32_t* emitted) {
         const uint32_t R = K() + 1;
         const bool greedy = sampling_is_greedy(samp);
-        std::vector<float> hid((size_t)R * d());
-        for (size_t b = 0; b < seqs.size(); b++) {
+        for_each_seq((int)seqs.size(), threads, [&](int b) {
+            std::vector<float> hid((size_t)R * d());
             Seq& s = seqs[b];
             std::vector<int32_t> in(R);
             in[0] = s.pending;
             for (uint32_t r = 1; r < R; r++) in[r] = s.drafts[r - 1];
             TierCache kv_keep = s.kv;
             SkipState sk_keep = s.skip;
-            const int64_t comp_keep = ffn_computed, skip_keep = ffn_skipped;
-            float* lg = last_logits.data() + b * R * V();
+            const int64_t comp_keep = s.ffn_computed, skip_keep = s.ffn_skipped;
+            float* lg = last_logits.data() + (size_t)b * R * V();
             for (uint32_t r = 0; r < R; r++)
                 forward_row(s, in[r], s.pos + r, lg + (size_t)r * V(), hid.data() + (size_t)r * d());
             uint32_t acc = 0;
@@ -952,8 +990,8 @@ struct Engine {
             // Commit rows 0..acc only (D7): replay them on the saved state.
             s.kv = std::move(kv_keep);
             s.skip = std::move(sk_keep);
-            ffn_computed = comp_keep;
-            ffn_skipped = skip_keep;
+            s.ffn_computed = comp_keep;
+            s.ffn_skipped = skip_keep;
             for (uint32_t r = 0; r <= acc; r++) forward_row(s, in[r], s.pos + r, nullptr, nullptr);
             if (n_emitted) n_emitted[b] = (int32_t)acc + 1;
             if (emitted) {
@@ -965,7 +1003,7 @@ struct Engine {
             s.pending = next;
             std::memcpy(s.hidden.data(), hid.data() + (size_t)acc * d(), d() * sizeof(float));
             draft(s);
-        }
+        });
     }
 };
 
@@ -1194,12 +1232,15 @@ void po_engine_read_mtp_logits(void* ep, float* out) {
     for (size_t b = 0; b < e->seqs.size(); b++)
         std::memcpy(out + b * n, e->seqs[b].mtp_logits.data(), n * sizeof(float));
 }
-float po_engine_skip_margin(void* ep) { return ((po::Engine*)ep)->skip_margin; }
+float po_engine_skip_margin(void* ep) { return ((po::Engine*)ep)->skip_margin(); }
 void po_engine_read_skip_counts(void* ep, int64_t* comp, int64_t* skip) {
     auto* e = (po::Engine*)ep;
-    *comp = e->ffn_computed;
-    *skip = e->ffn_skipped;
+    *comp = e->ffn_computed();
+    *skip = e->ffn_skipped();
 }
+// Host threads over sequences for prefill and step (1: one after another;
+// the results do not depend on it).
+void po_engine_set_threads(void* ep, int threads) { ((po::Engine*)ep)->threads = std::max(1, threads); }
 uint32_t po_engine_read_kv(void* ep, int32_t b, uint32_t l, uint32_t h, int8_t* k, float* ks, int8_t* v,
                            float* vs, uint32_t max_n) {
     auto* e = (po::Engine*)ep;

@@ -181,7 +181,8 @@ __device__ __forceinline__ float col_value(const int32_t (&a)[P], float a_s, flo
     } else if constexpr (EPI == EPI_LOGITS3) {
         return __fmul_rn(comb3<P>(a), s_all);
     } else if constexpr (EPI == EPI_MTP_SWIGLU3 || EPI == EPI_MTP_RESID3) {
-        return __fmul_rn(__fmul_rn(comb3<P>(a), a_s), w_s);
+        // scales first: a_s * w_s stays finite where comb * a_s may not
+        return __fmul_rn(comb3<P>(a), __fmul_rn(a_s, w_s));
     } else {
         return __fmul_rn(__fmul_rn(__int2float_rn(a[0]), a_s), w_s);
     }

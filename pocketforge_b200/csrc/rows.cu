@@ -257,13 +257,16 @@ __global__ void __launch_bounds__(RT) split_digits_kernel(const float* __restric
     const float* xr = x + (size_t)row * ldx;
     float v[EPT];
     float amax = 0.0f;
+    int bad = 0;  // a NaN or inf in this thread's part of the row (fmaxf drops NaN)
 #pragma unroll
     for (int i = 0; i < EPT; i++) {
         const int c = t + i * RT;
         v[i] = c < n ? xr[c] : 0.0f;
         amax = fmaxf(amax, fabsf(v[i]));
+        bad |= !isfinite(v[i]);
     }
     amax = block_max(amax, sh);
+    if (__syncthreads_or(bad)) amax = __int_as_float(0x7fc00000);
     const float mul = (amax == 0.0f || !isfinite(amax)) ? 0.0f : __fdiv_rn(127.0f, amax);
 #pragma unroll
     for (int i = 0; i < EPT; i++) {
@@ -358,23 +361,32 @@ __global__ void __launch_bounds__(RT) mtp_finish_kernel(const int32_t* __restric
     };
     float v[E];
     float amax = 0.0f;
+    int bad = 0;  // a NaN or inf in this thread's columns (fmaxf drops NaN)
 #pragma unroll
     for (int i = 0; i < E; i++) {
         const int c = t + i * RT;
         v[i] = 0.0f;
         if (c >= d) continue;
+        // The two scales are multiplied first: the chained heads can grow the
+        // hidden state to ~1e35, where sum * a_scale alone would overflow
+        // although the product with the (small) weight scale is finite, as
+        // the reference's float dot product of h with the dequantized row is.
         if constexpr (SWIGLU) {
-            const float g = __fmul_rn(__fmul_rn(comb3(acc[i][0][0], acc[i][1][0], acc[i][2][0]), as), ws[i][0]);
-            const float u = __fmul_rn(__fmul_rn(comb3(acc[i][0][1], acc[i][1][1], acc[i][2][1]), as), ws[i][1]);
+            const float g = __fmul_rn(comb3(acc[i][0][0], acc[i][1][0], acc[i][2][0]), __fmul_rn(as, ws[i][0]));
+            const float u = __fmul_rn(comb3(acc[i][0][1], acc[i][1][1], acc[i][2][1]), __fmul_rn(as, ws[i][1]));
             v[i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);  // the GEMM epilogue's mtp_swiglu
         } else {
-            v[i] = __fadd_rn(xr[i], __fmul_rn(__fmul_rn(comb3(acc[i][0][0], acc[i][1][0], acc[i][2][0]), as), ws[i][0]));
+            v[i] = __fadd_rn(xr[i], __fmul_rn(comb3(acc[i][0][0], acc[i][1][0], acc[i][2][0]), __fmul_rn(as, ws[i][0])));
             x[(size_t)row * d + c] = v[i];
         }
         amax = fmaxf(amax, fabsf(v[i]));
+        bad |= !isfinite(v[i]);
     }
-    // digit planes of the row, as split_digits_kernel
+    // digit planes of the row, as split_digits_kernel; a row holding NaN or
+    // inf gets a NaN scale, so every product over it is NaN, as the
+    // reference's float dot products over such a row are
     amax = block_max(amax, sh);
+    if (__syncthreads_or(bad)) amax = __int_as_float(0x7fc00000);
     const float mul = (amax == 0.0f || !isfinite(amax)) ? 0.0f : __fdiv_rn(127.0f, amax);
     const size_t plane = (size_t)M * d;
 #pragma unroll

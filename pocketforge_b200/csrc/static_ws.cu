@@ -15,11 +15,12 @@
 // contents, so each call clears the part it uses on the caller's stream
 // before launching; two calls whose work overlaps on the GPU (different
 // streams, no ordering between them) race on it and must not be issued.
-// The first call on a device looks up the array's device address
-// (cudaGetSymbolAddress) and clears it synchronously; make that first call
-// before any stream capture.
-#include <mutex>
-
+// Every call looks up the array's device address (cudaGetSymbolAddress) with
+// the caller's device current.  The first lookup on a device loads the
+// module there, so make the first call before any stream capture.  Later
+// lookups are cheap, and looking up every time keeps a call after
+// cudaDeviceReset (which unloads the module; the array may come back at
+// another address) from writing through a stale pointer.
 #include "gemm.cuh"
 #include "gemm_tc.cuh"
 
@@ -27,7 +28,7 @@ namespace pf {
 namespace {
 
 constexpr size_t kStaticWsElems = (size_t)1 << 20;  // int32 partial sums: M*N <= 1,048,576
-constexpr int kStaticCounters = 4096;                // split-K tiles: ceil(M/64)*(N/64) <= 4096
+constexpr int kStaticCounters = 4096;                // split-K tiles: ceil(M/128)*ceil(N/64) <= 4096
 
 static __device__ __align__(256) int32_t g_split_ws[kStaticWsElems];
 static __device__ __align__(256) int g_split_cnt[kStaticCounters];
@@ -38,26 +39,14 @@ struct StaticAddr {
 };
 
 pf_status static_addr(StaticAddr* out) {
-    static std::mutex mu;
-    static StaticAddr addr[64];
-    int dev = 0;
-    PF_CUDA(cudaGetDevice(&dev));
-    PF_CHECK(dev >= 0 && dev < 64, "device index %d out of range", dev);
-    std::lock_guard<std::mutex> lk(mu);
-    if (!addr[dev].ws) {
-        // In host code g_split_ws names a host-side shadow, not device memory:
-        // the kernel gets the address the device sees.
-        void* ws = nullptr;
-        void* cnt = nullptr;
-        PF_CUDA(cudaGetSymbolAddress(&ws, g_split_ws));
-        PF_CUDA(cudaGetSymbolAddress(&cnt, g_split_cnt));
-        PF_CUDA(cudaMemset(ws, 0, kStaticWsElems * sizeof(int32_t)));
-        PF_CUDA(cudaMemset(cnt, 0, kStaticCounters * sizeof(int)));
-        PF_CUDA(cudaDeviceSynchronize());
-        addr[dev].ws = static_cast<int32_t*>(ws);
-        addr[dev].cnt = static_cast<int*>(cnt);
-    }
-    *out = addr[dev];
+    // In host code g_split_ws names a host-side shadow, not device memory:
+    // the kernel gets the address the device sees.
+    void* ws = nullptr;
+    void* cnt = nullptr;
+    PF_CUDA(cudaGetSymbolAddress(&ws, g_split_ws));
+    PF_CUDA(cudaGetSymbolAddress(&cnt, g_split_cnt));
+    out->ws = static_cast<int32_t*>(ws);
+    out->cnt = static_cast<int*>(cnt);
     return PF_OK;
 }
 
@@ -70,8 +59,10 @@ extern "C" pf_status pf_gemm_packed_static(const int8_t* Aq, const float* a_scal
                                            const float* w_scale, int32_t qtype, float* C, int32_t M, int32_t N,
                                            int32_t K, void* stream) {
     PF_TRY(require_device());
+    PF_CHECK(M >= 0, "pf_gemm_packed_static: M=%d", M);
+    if (M == 0) return PF_OK;  // no rows: nothing to compute (as pf_gemm_packed)
     PF_CHECK(Aq && a_scale && packed_w && C, "pf_gemm_packed_static: null argument");
-    PF_CHECK(M > 0 && N > 0 && K > 0, "pf_gemm_packed_static: empty shape");
+    PF_CHECK(N > 0 && K > 0, "pf_gemm_packed_static: empty shape");
     PF_CHECK((size_t)M * (size_t)N <= kStaticWsElems,
              "pf_gemm_packed_static: M*N = %lld exceeds the static workspace of %zu partial sums",
              (long long)M * N, kStaticWsElems);
@@ -92,7 +83,9 @@ extern "C" pf_status pf_gemm_packed_static(const int8_t* Aq, const float* a_scal
     p.ws_elems = kStaticWsElems;
     p.cnt_elems = kStaticCounters;
     // The kernel leaves the workspace zeroed, but an earlier call that did not
-    // complete may not have: clear what this call reads before its first use.
+    // complete may not have: clear what this call reads before its first use
+    // (the partial sums [n][m] and the counters of every tile index the launch
+    // can form, ceil(M/128) * N/BN <= tiles).
     PF_CUDA(cudaMemsetAsync(a.ws, 0, (size_t)M * N * sizeof(int32_t), st));
     PF_CUDA(cudaMemsetAsync(a.cnt, 0, tiles * sizeof(int), st));
     return gemm_tc_launch(p, 1, M, st);

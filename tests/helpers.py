@@ -3,6 +3,7 @@ a small wrapper over the oracle's Level-B engine (test infrastructure)."""
 from __future__ import annotations
 
 import ctypes as C
+import os
 from dataclasses import dataclass, field, replace
 from typing import Optional
 
@@ -80,18 +81,36 @@ def make_weights(cfg: Cfg, seed: int = 0, mtp_seed: int = 3):
     return w
 
 
+def host_threads() -> int:
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except AttributeError:
+        return max(1, os.cpu_count() or 1)
+
+
 class OracleEngine:
-    def __init__(self, cfg: Cfg, weights, order: int = 1, sampling=None, skip_threshold=None):
+    """weights: a make_weights() dict, or None for the synthetic model of the
+    benchmark configurations (seed 0 / MTP seed 3, the generator both sides
+    restate).  Sequences run on `threads` host threads (results do not
+    depend on it)."""
+
+    def __init__(self, cfg: Cfg, weights, order: int = 1, sampling=None, skip_threshold=None, threads=None,
+                 seed: int = 0, mtp_seed: int = 3):
         self.cfg = cfg
         self.L = oracle.lib()
         self._c = cfg.oracle_c()
         self.h = self.L.po_engine_create(C.byref(self._c))
         self.L.po_engine_set_order(self.h, order)
+        self.L.po_engine_set_threads(self.h, threads or host_threads())
         if sampling is not None:
             self._s = oracle.PfSamplingConfig(*sampling)
             self.L.po_engine_set_sampling(self.h, C.byref(self._s))
         if skip_threshold is not None:
             self.L.po_engine_set_skip_threshold(self.h, skip_threshold)
+        self.n = 0
+        if weights is None:
+            self.L.po_engine_load_synthetic(self.h, seed, mtp_seed, threads or host_threads())
+            return
         for l in range(cfg.n_layers):
             for m in range(7):
                 a, rs = weights[(l, m)]

@@ -16,7 +16,7 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-from helpers import Cfg, OracleEngine, make_weights, prompts  # noqa: E402
+from helpers import Cfg, OracleEngine, host_threads, make_weights, prompts  # noqa: E402
 
 import pocketforge_b200 as pf  # noqa: E402
 
@@ -30,16 +30,21 @@ def need_device():
 
 
 def gpu_engine(cfg: Cfg, w, max_seqs, max_pos, sampling=None, skip_threshold=None, attn_splits=0):
+    """w: a make_weights() dict, or None for the synthetic benchmark model
+    (seed 0, MTP seed 3) generated on both sides."""
     e = pf.BatchEngine(cfg.product(), max_seqs, max_pos)
     e.set_attention_splits(attn_splits)
-    for l in range(cfg.n_layers):
-        for m in range(7):
-            a, rs = w[(l, m)]
-            e.set_matrix(l, m, a, rs)
-    emb, gs = w["emb"]
-    e.set_embedding(emb, gs)
-    for h in range(cfg.n_mtp_heads):
-        e.set_mtp_head(h, *w[("mtp", h)])
+    if w is None:
+        e.load_synthetic(seed=0, mtp_seed=3, threads=host_threads())
+    else:
+        for l in range(cfg.n_layers):
+            for m in range(7):
+                a, rs = w[(l, m)]
+                e.set_matrix(l, m, a, rs)
+        emb, gs = w["emb"]
+        e.set_embedding(emb, gs)
+        for h in range(cfg.n_mtp_heads):
+            e.set_mtp_head(h, *w[("mtp", h)])
     if sampling is not None:
         e.set_sampling(*sampling)
     if skip_threshold is not None:
@@ -47,16 +52,37 @@ def gpu_engine(cfg: Cfg, w, max_seqs, max_pos, sampling=None, skip_threshold=Non
     return e
 
 
+FLT_MAX = float(np.finfo(np.float32).max)
+
+
 def rel_err(a, b):
-    """Largest |a-b| relative to the row's largest finite magnitude.  Rows the
-    synthetic model drives past float range (the chained MTP heads overflow on
-    it, in the reference arithmetic too) must be non-finite on both sides."""
-    fa, fb = np.isfinite(a), np.isfinite(b)
-    assert (fa == fb).mean() >= 0.999, "non-finite pattern differs"
+    """Largest |a-b| relative to the row's largest finite magnitude, over the
+    rows (last axis) that are finite on both sides.
+
+    Rows the synthetic model drives past float range (the chained MTP heads
+    overflow on it, in the reference arithmetic too) hold a non-finite element
+    on both sides; their remaining values are meaningless and are not compared
+    (nor are the drafts drawn from them).  A row may overflow on one side only
+    at the edge of float range: the other side's largest magnitude within
+    RTOL of FLT_MAX (two results 1e-7 apart there round to either side of the
+    overflow)."""
+    a2 = a.reshape(-1, a.shape[-1])
+    b2 = b.reshape(-1, b.shape[-1])
+    ra, rb = np.isfinite(a2).all(axis=-1), np.isfinite(b2).all(axis=-1)
+    for r in np.nonzero(ra != rb)[0]:
+        fin = a2[r] if ra[r] else b2[r]
+        top = float(np.abs(fin).max())
+        print(f"row {r} overflowed on one side only; the other side's largest magnitude is {top:.6g}")
+        assert top >= FLT_MAX * (1 - RTOL), "a row overflowed on one side only, away from the edge of float range"
+    keep = ra & rb
+    if not keep.any():
+        return 0.0
+    a2, b2 = a2[keep], b2[keep]
+    fa, fb = np.isfinite(a2), np.isfinite(b2)
     both = fa & fb
-    bm = np.where(both, np.abs(b), 0.0)
+    bm = np.where(both, np.abs(b2), 0.0)
     scale = np.maximum(bm.max(axis=-1, keepdims=True), 1e-30)
-    d = np.where(both, np.abs(a - b), 0.0) / scale
+    d = np.where(both, np.abs(a2 - b2), 0.0) / scale
     return float(d.max()) if d.size else 0.0
 
 

@@ -57,6 +57,16 @@ def test_static_workspace_matches_allocating_path(qtype, lo, hi, M, N, K):
         np.testing.assert_array_equal(out.cpu().numpy().view(np.uint32), ref.cpu().numpy().view(np.uint32))
 
 
+def test_static_workspace_empty_batch_is_a_no_op():
+    """M = 0 returns PF_OK without touching the output, as pf_gemm_packed does."""
+    if pf.device_count() == 0:
+        pytest.skip("no sm_100 device")
+    L = _bind()
+    st = L.pf_gemm_packed_static(C.c_void_p(16), C.c_void_p(16), C.c_void_p(16), C.c_void_p(16), 1, C.c_void_p(16),
+                                 0, 2048, 2048, None)
+    assert st == 0
+
+
 def test_static_workspace_rejects_oversize():
     if pf.device_count() == 0:
         pytest.skip("no sm_100 device")
