@@ -203,6 +203,9 @@ def ref():
         _sig(L, "pfref_quantize_matrix", u64, _f32p, u32, u32, C.c_int, vp)
         _sig(L, "pfref_squeeze_roundtrip", C.c_int, C.c_char_p, _f32p, u32, u32, C.c_int, _i8p,
              _f32p, _f32p)
+        _sig(L, "pfref_write_squeeze_model", C.c_int, C.c_char_p, u32, u32, u32, u32, u32, u32, u32, u32, _f32p,
+             np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS"))
+        _sig(L, "pfref_load_block", C.c_int64, C.c_char_p, u32, u32, _i8p, _f32p, _f32p, C.c_int64)
         _sig(L, "pfref_engine_create", vp)
         _sig(L, "pfref_engine_destroy", None, vp)
         _sig(L, "pfref_seed_sampler", None, u32)

@@ -214,6 +214,68 @@ int pfref_write_model(const char* path, uint32_t n_layers, uint32_t d, uint32_t 
     return q.write_squeeze(path, {b}, {comp}, c) ? 0 : -1;
 }
 
+// A whole model through the reference's own writer: every layer matrix
+// (layer-major, matrices 0..6 in ModelConfig order: q, k, v, o, gate, up,
+// down) and the tied embedding (0,10) quantized by Quantizer::quantize_matrix
+// with its format (qtypes[0..6] per matrix, qtypes[7] for the embedding),
+// zstd-compressed by compress_block and written by write_squeeze.  `mats`
+// holds the float matrices back to back in that order.
+int pfref_write_squeeze_model(const char* path, uint32_t n_layers, uint32_t d, uint32_t heads, uint32_t kv_heads,
+                              uint32_t ff, uint32_t vocab, uint32_t max_seq, uint32_t mtp_heads, const float* mats,
+                              const int* qtypes) {
+    forge::ModelConfig c;
+    c.n_layers = n_layers;
+    c.n_embd = d;
+    c.n_heads = heads;
+    c.n_kv_heads = kv_heads;
+    c.n_ff = ff;
+    c.n_vocab = vocab;
+    c.max_seq_len = max_seq;
+    c.mtp_heads = mtp_heads;
+    forge::Quantizer q(c);
+    const uint32_t hd = d / heads;
+    const uint32_t rows[7] = {heads * hd, kv_heads * hd, kv_heads * hd, d, ff, ff, d};
+    const uint32_t cols[7] = {d, d, d, heads * hd, d, d, ff};
+    std::vector<forge::WeightBlock> blocks;
+    std::vector<std::vector<uint8_t>> data;
+    size_t off = 0;
+    auto add = [&](uint32_t layer, uint32_t m, uint32_t r, uint32_t cc, int qt) {
+        auto qd = q.quantize_matrix(mats + off, r, cc, (uint8_t)qt);
+        off += (size_t)r * cc;
+        auto comp = q.compress_block(qd);
+        forge::WeightBlock b{};
+        b.layer_id = layer;
+        b.matrix_id = m;
+        b.n_rows = r;
+        b.n_cols = cc;
+        b.compressed_size = (uint32_t)comp.size();
+        b.original_size = (uint32_t)qd.size();
+        b.quant_type = (uint8_t)qt;
+        blocks.push_back(b);
+        data.push_back(std::move(comp));
+    };
+    for (uint32_t l = 0; l < n_layers; l++)
+        for (uint32_t m = 0; m < 7; m++) add(l, m, rows[m], cols[m], qtypes[m]);
+    add(0, 10, vocab, d, qtypes[7]);
+    return q.write_squeeze(path, blocks, data, c) ? 0 : -1;
+}
+
+// One block of a .squeeze file as WeightLoader::load_block_with_scales returns
+// it: int8 values [rows * cols], row scales [rows] and the global scale.
+// Returns the number of values, or a negative code.
+int64_t pfref_load_block(const char* path, uint32_t layer, uint32_t matrix, int8_t* out, float* row_scales,
+                         float* global_scale, int64_t max_values) {
+    forge::WeightLoader ld;
+    if (!ld.open(path)) return -1;
+    auto r = ld.load_block_with_scales(layer, matrix);
+    if (r.data.empty()) return -2;
+    if ((int64_t)r.data.size() > max_values) return -3;
+    std::memcpy(out, r.data.data(), r.data.size());
+    std::memcpy(row_scales, r.row_scales.data(), r.row_scales.size() * sizeof(float));
+    *global_scale = r.global_scale;
+    return (int64_t)r.data.size();
+}
+
 // Engine::generate on one prompt; returns the number of generated tokens and
 // the engine's own tokens_per_second (which counts prompt tokens).
 int pfref_literal_generate(const char* path, const int32_t* prompt, uint32_t n, uint32_t max_new, int32_t* out,

@@ -64,6 +64,7 @@ constexpr int NW = 4;    // warps per CTA
 constexpr int NSW = 3;   // cp.async stages per warp
 constexpr int BIG = 1 << 30;
 constexpr int PART = 68; // floats per (split, row) partial state: m, l, pad, pad, o[64]
+constexpr int kMaxSplits = 8;  // context splits per (sequence, kv head, row group)
 constexpr int NEXMAX = 4; // extra blocks (sinks, in-batch pool entries, earlier rows of the batch)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kMaxLead = 8.0f;  // log2 units a block max may exceed the reference before it moves
@@ -716,16 +717,30 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
             o0 = sm.u.merge.acc[0][ri][lane] * f;
             o1 = sm.u.merge.acc[0][ri][lane + 32] * f;
         } else {
+            // every split's state of the row is loaded before any is used
             const float* part = aw.part + item * nsplit * QR * PART + (size_t)ri * PART;
-            for (int sp2 = 0; sp2 < nsplit; sp2++) m = fmaxf(m, __ldcg(part + (size_t)sp2 * QR * PART));
+            float mc[kMaxSplits], lc[kMaxSplits], oa[kMaxSplits], ob[kMaxSplits];
+#pragma unroll
+            for (int sp2 = 0; sp2 < kMaxSplits; sp2++) {
+                mc[sp2] = -INFINITY;
+                lc[sp2] = oa[sp2] = ob[sp2] = 0.0f;
+                if (sp2 < nsplit) {
+                    const float* pr = part + (size_t)sp2 * QR * PART;
+                    mc[sp2] = __ldcg(pr);
+                    lc[sp2] = __ldcg(pr + 1);
+                    oa[sp2] = __ldcg(pr + 4 + lane);
+                    ob[sp2] = __ldcg(pr + 4 + lane + 32);
+                }
+            }
+#pragma unroll
+            for (int sp2 = 0; sp2 < kMaxSplits; sp2++) m = fmaxf(m, mc[sp2]);
             l = 0.0f, o0 = 0.0f, o1 = 0.0f;
-            for (int sp2 = 0; sp2 < nsplit; sp2++) {
-                const float* pr = part + (size_t)sp2 * QR * PART;
-                const float mc = __ldcg(pr);
-                const float f = (mc == -INFINITY) ? 0.0f : ex2((mc - m) * fq);
-                l += __ldcg(pr + 1) * f;
-                o0 += __ldcg(pr + 4 + lane) * f;
-                o1 += __ldcg(pr + 4 + lane + 32) * f;
+#pragma unroll
+            for (int sp2 = 0; sp2 < kMaxSplits; sp2++) {
+                const float f = (mc[sp2] == -INFINITY) ? 0.0f : ex2((mc[sp2] - m) * fq);
+                l += lc[sp2] * f;
+                o0 += oa[sp2] * f;
+                o1 += ob[sp2] * f;
             }
         }
         const float ps = ex2((ss - m) * fq);
@@ -789,7 +804,8 @@ pf_status attention_decode(const KvCache& kv, int layer, const RowBatch& rb, con
     PF_CHECK(kv.hd == 64, "attention_decode: head_dim must be 64");
     PF_CHECK(attention_decode_supported(kv, H, rb.max_rows), "attention_decode: too many query rows");
     const int nrg = attention_decode_row_groups(kv, H, rb.max_rows);
-    PF_CHECK(aw.nsplit >= 1 && aw.nsplit * nrg <= 65535, "attention_decode: bad split count");
+    PF_CHECK(aw.nsplit >= 1 && aw.nsplit <= kMaxSplits && aw.nsplit * nrg <= 65535,
+             "attention_decode: %d context splits (1..%d)", aw.nsplit, kMaxSplits);
     PF_CHECK(aw.nsplit == 1 ||
                  (aw.part && aw.cnt && aw.part_floats >= attention_decode_work_floats(rb.nb, kv.G, aw.nsplit, nrg) &&
                   aw.cnt_elems >= (size_t)rb.nb * kv.G * nrg),

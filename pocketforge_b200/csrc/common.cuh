@@ -22,6 +22,7 @@ const char* last_error();
         if (_e != cudaSuccess) {                                                        \
             ::pf::set_error("%s:%d %s: %s", __FILE__, __LINE__, #call,                  \
                             cudaGetErrorString(_e));                                    \
+            cudaGetLastError(); /* not reported again by the next launch check */       \
             return PF_ERR_CUDA;                                                         \
         }                                                                               \
     } while (0)

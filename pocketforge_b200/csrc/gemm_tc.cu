@@ -768,6 +768,7 @@ pf_status gemm_tc_launch(const GemmParams& p0, int planes, int plane_rows, cudaS
              "gemm_tc: plane layout must be [planes][plane_rows][lda]");
     const bool three = p.epi == EPI_LOGITS3 || p.epi == EPI_MTP_SWIGLU3 || p.epi == EPI_MTP_RESID3;
     PF_CHECK(three == (planes == 3), "gemm_tc: epilogue %d does not take %d planes", p.epi, planes);
+    if (gemv_applies(p, planes)) return gemv_launch(p, planes, st);  // a few rows: dp4a, weights streamed once
     const int bn = gemm_tc_pick_bn(p.M, p.N, planes);
     if (p.slice_stride > 0) {  // split K into separate int32 slices, reduced by the caller's next kernel
         PF_CHECK(p.epi == EPI_I32 && planes == 1 && p.splits >= 1 && p.splits <= p.K / BK,

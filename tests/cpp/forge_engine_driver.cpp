@@ -1,5 +1,6 @@
 // Drives the forge:: C++ engines for tests/test_forge_engine.py:
-//   forge_engine_driver <model.squeeze> <max_new> <prompt tokens...>
+//   forge_engine_driver <model.squeeze> <max_new> [q=Q,K,V,O,GATE,UP,DOWN,EMB] <prompt tokens...>
+// (q=: the file's quantization types for forge::BatchEngine, default all Q8)
 // prints "engine: <tokens>" from forge::Engine::generate (greedy) and
 // "batch <i>: <tokens>" from forge::BatchEngine::generate with the same
 // prompt twice plus a shifted copy, then "forward: <argmax>".
@@ -13,8 +14,19 @@
 int main(int argc, char** argv) {
     if (argc < 4) return 2;
     const uint32_t max_new = (uint32_t)std::atoi(argv[2]);
+    int qt[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int first = 3;
+    if (argv[3][0] == 'q' && argv[3][1] == '=') {
+        const char* s = argv[3] + 2;
+        for (int i = 0; i < 8 && *s; i++) {
+            qt[i] = std::atoi(s);
+            while (*s && *s != ',') s++;
+            if (*s == ',') s++;
+        }
+        first = 4;
+    }
     std::vector<int32_t> prompt;
-    for (int i = 3; i < argc; i++) prompt.push_back(std::atoi(argv[i]));
+    for (int i = first; i < argc; i++) prompt.push_back(std::atoi(argv[i]));
 
     forge::Engine e;
     e.set_max_context(512);
@@ -35,8 +47,8 @@ int main(int argc, char** argv) {
     bc.model = e.config();
     bc.max_context = 512;
     bc.model.kv_cache_size = 512;
-    for (int i = 0; i < 7; i++) bc.qtype[i] = 0;
-    bc.emb_qtype = 0;
+    for (int i = 0; i < 7; i++) bc.qtype[i] = qt[i];
+    bc.emb_qtype = qt[7];
     forge::BatchEngine b(bc, 3, 512, 0);
     if (!b.ok() || !b.load_squeeze(argv[1])) {
         std::printf("batch load failed: %s\n", b.last_error().c_str());

@@ -142,3 +142,81 @@ def test_cpp_engines_match_oracle():
     assert [int(t) for t in lines["batch 0"]] == want
     assert [int(t) for t in lines["batch 2"]] == want
     assert int(lines["forward"][0]) == want[0] and int(lines["forward"][1]) == cfg.n_vocab
+
+
+# (attention q, k, v, o, gate, up, down, embedding) quantization types:
+# 0 Q8, 1 Q4, 2 Q2, 3 Q1.5 (the reference's per-matrix formats)
+REF_FORMATS = {"q4": [1, 1, 1, 1, 1, 1, 1, 1], "q2_q15_mix": [1, 1, 1, 1, 2, 2, 3, 1],
+               "q8": [0, 0, 0, 0, 0, 0, 0, 0]}
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt", sorted(REF_FORMATS))
+def test_reference_written_squeeze_matches_oracle(rlib, fmt):
+    """A .squeeze file written by the reference's own Quantizer::quantize_matrix,
+    compress_block and write_squeeze (oracle/_ref, compiled from its sources)
+    from N(0, 0.02) weights, loaded by forge::Engine::load_model and
+    forge::BatchEngine::load_squeeze.  The oracle gets exactly what the
+    reference's WeightLoader::load_block_with_scales decodes from the same file
+    (Q4 / Q2 streams decoded from their first byte, scales 1; Q8 row scales
+    the mean of the block scales).  Greedy token streams must match."""
+    qt = REF_FORMATS[fmt]
+    cfg = Cfg(n_mtp_heads=2, qtype=qt[:7], emb_qtype=qt[7], window_size=512, max_context=512)
+    rng = np.random.default_rng(21)
+    shapes = [cfg.shape(m) for m in range(7)]
+    mats = [rng.normal(0.0, 0.02, shapes[m]).astype(np.float32) for _ in range(cfg.n_layers) for m in range(7)]
+    mats.append(rng.normal(0.0, 0.02, (cfg.n_vocab, cfg.n_embd)).astype(np.float32))
+    flat = np.ascontiguousarray(np.concatenate([m.ravel() for m in mats]))
+    prompt = [5, 17, 200, 33, 9, 120]
+    max_new = 12
+    import oracle
+    L = oracle.lib()
+    with tempfile.TemporaryDirectory() as td:
+        path = os.path.join(td, "ref.squeeze")
+        assert rlib.pfref_write_squeeze_model(path.encode(), cfg.n_layers, cfg.n_embd, cfg.n_heads, cfg.n_kv_heads,
+                                              cfg.n_ff, cfg.n_vocab, 512, cfg.n_mtp_heads, flat,
+                                              np.asarray(qt, np.int32)) == 0
+        weights = {}
+
+        def load(layer, m, rows, cols):
+            out = np.zeros(rows * cols, np.int8)
+            rs = np.zeros(rows, np.float32)
+            gs = np.zeros(1, np.float32)
+            assert rlib.pfref_load_block(path.encode(), layer, m, out, rs, gs, rows * cols) == rows * cols
+            return out.reshape(rows, cols), rs, float(gs[0])
+
+        for l in range(cfg.n_layers):
+            for m in range(7):
+                a, rs, _ = load(l, m, *shapes[m])
+                weights[(l, m)] = (a, rs)
+        qe, _, gs = load(0, 10, cfg.n_vocab, cfg.n_embd)
+        weights["emb"] = (qe, gs)
+        d = cfg.n_embd
+        for h in range(cfg.n_mtp_heads):  # the engines' MTP heads: seeded generator, seed 3
+            parts = []
+            for j in range(3):
+                qq = np.zeros(d * d // 2, np.uint8)
+                s = np.zeros(d, np.float32)
+                L.po_synth_mtp_matrix(3, h, j, d, qq, s)
+                parts += [qq, s]
+            weights[("mtp", h)] = parts
+        exe = os.path.join(td, "driver")
+        lib_dir = os.path.join(ROOT, "pocketforge_b200")
+        subprocess.run(["g++", "-O1", "-std=c++17", "-I" + os.path.join(ROOT, "include"),
+                        os.path.join(ROOT, "tests", "cpp", "forge_engine_driver.cpp"), "-o", exe,
+                        "-L" + lib_dir, "-l:libforge_b200.so", "-Wl,-rpath," + lib_dir], check=True)
+        out = subprocess.run([exe, path, str(max_new), "q=" + ",".join(map(str, qt)), *map(str, prompt)],
+                             capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stdout + out.stderr
+    lines = {ln.split(":")[0]: ln.split(":", 1)[1].split() for ln in out.stdout.splitlines() if ":" in ln}
+
+    o = OracleEngine(cfg, weights)
+    o.prefill([prompt])
+    want = [int(o.pending()[0])]
+    while len(want) < max_new:
+        n, em = o.step()
+        want += [int(t) for t in em[0, : n[0]]]
+    want = want[:max_new]
+    assert [int(t) for t in lines["engine"]] == want
+    assert [int(t) for t in lines["batch 0"]] == want
+    assert [int(t) for t in lines["batch 2"]] == want

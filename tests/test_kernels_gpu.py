@@ -127,6 +127,31 @@ def test_packed_projection_bitexact(qtype, lo, hi, M, N, K):
     np.testing.assert_array_equal(Cd.cpu().numpy().view(np.uint32), want.astype(np.float32).view(np.uint32))
 
 
+@pytest.mark.parametrize("qtype,lo,hi", [(1, -8, 8), (2, -2, 2), (0, -128, 128)])
+@pytest.mark.parametrize("M", [1, 5, 16])
+@pytest.mark.parametrize("N,K", [(2048, 2048), (3072, 2048), (2048, 5632), (11264, 2048)])
+def test_few_row_projection_bitexact(olib, qtype, lo, hi, M, N, K):
+    """At most 16 activation rows run on the dp4a path (gemv.cu): the same
+    int32 sums and matmul_quantized epilogue as the oracle, bit for bit."""
+    rng = np.random.default_rng(qtype * 1000 + M * 7 + N + K)
+    W = rng.integers(lo, hi, (N, K), dtype=np.int8)
+    Af = (rng.standard_normal((M, K)) * 3).astype(np.float32)
+    ws = rng.uniform(0.5, 2, N).astype(np.float32)
+    A = np.zeros((M, K), np.int8)
+    a_s = np.zeros(M, np.float32)
+    for i in range(M):
+        q, s = np.zeros(K, np.int8), np.zeros(1, np.float32)
+        olib.po_quantize_activation_row(np.ascontiguousarray(Af[i]), q, s, K)
+        A[i], a_s[i] = q, s[0]
+    packed = torch.zeros(_lib.lib().pf_packed_weight_bytes(N, K, qtype), dtype=torch.uint8, device="cuda")
+    call("pf_pack_weights", p(dev(W)), N, K, qtype, p(packed), None)
+    Cd = torch.zeros((M, N), device="cuda")
+    call("pf_gemm_packed", p(dev(A)), p(dev(a_s)), p(packed), p(dev(ws)), qtype, p(Cd), M, N, K, None)
+    want = np.zeros(M * N, np.float32)
+    olib.po_matmul_quantized(Af.ravel(), W.ravel(), want, M, N, K, ws, None)
+    np.testing.assert_array_equal(Cd.cpu().numpy().ravel().view(np.uint32), want.view(np.uint32))
+
+
 def test_pack_rejects_out_of_range():
     W = np.full((8, 128), 9, np.int8)  # 9 does not fit Q4
     packed = torch.zeros(_lib.lib().pf_packed_weight_bytes(8, 128, 1), dtype=torch.uint8, device="cuda")

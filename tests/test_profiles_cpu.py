@@ -24,6 +24,14 @@ def test_summary_commands_follow_the_rules(name):
     for cmd in commands:
         assert "--clock-control none" in cmd, cmd
         assert re.search(r"\bpython bench\.py\b", cmd), cmd
+        # Anything beyond the one-pass launch list (more metrics, sections,
+        # sets) replays each captured launch several times: such captures
+        # name one kernel and a few launches.
+        m = re.search(r"--metrics\s+(\S+)", cmd)
+        heavy = ("--set" in cmd or "--section" in cmd or (m is not None and m.group(1) != "gpu__time_duration.sum"))
+        if heavy:
+            assert re.search(r"(^|\s)-k\s", cmd) and re.search(r"(^|\s)-c\s+[1-3]\b", cmd), \
+                f"a multi-pass capture must select one kernel (-k) and 1-3 launches (-c): {cmd}"
     for ln in text.splitlines():
         if ln.startswith("bench-traffic:"):
             parts = ln.split()
