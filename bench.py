@@ -162,9 +162,11 @@ def projection_ops_per_step(model, M, B, K):
     return layers + unembed + mtp
 
 
-def cpu_baseline(model, seconds_budget=25.0, threads=8):
-    """The oracle port (CPU restatement of the Level-B step, one core) on a
-    bounded sample: 1 sequence, 4-token prompt, decode steps until ~budget."""
+def cpu_baseline(model, prompt_len, seconds_budget=20.0):
+    """The oracle port (CPU restatement of the Level-B step) timed on one core
+    on a bounded sample of the workload: 1 sequence at the config's context —
+    its prompt prefilled first, untimed, on all host cores — then decode
+    steps on one thread until ~budget."""
     import ctypes as C
 
     import oracle
@@ -177,11 +179,16 @@ def cpu_baseline(model, seconds_budget=25.0, threads=8):
                 c.qtype[i] = q
         else:
             setattr(c, name, type(getattr(c, name))(getattr(model, name)))
+    host = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
     e = L.po_engine_create(C.byref(c))
     try:
-        L.po_engine_load_synthetic(e, 0, 3, threads)
-        toks = np.arange(4, dtype=np.int32)
-        L.po_engine_prefill(e, 1, toks, np.array([0, 4], np.int64), None)
+        L.po_engine_load_synthetic(e, 0, 3, host)
+        toks = make_prompts([0], prompt_len, model.n_vocab)[0]
+        t_pre = time.perf_counter()
+        L.po_engine_set_prefill_threads(e, host)
+        L.po_engine_prefill(e, 1, toks, np.array([0, prompt_len], np.int64), None)
+        L.po_engine_set_prefill_threads(e, 1)
+        t_pre = time.perf_counter() - t_pre
         n = np.zeros(1, np.int32)
         em = np.zeros(model.n_mtp_heads + 1, np.int32)
         gen, steps, t0 = 0, 0, time.perf_counter()
@@ -193,8 +200,9 @@ def cpu_baseline(model, seconds_budget=25.0, threads=8):
             if el > seconds_budget or steps >= 8:
                 break
         return {"value": gen / el, "unit": UNIT, "cores": 1, "kind": "port",
-                "sample": f"oracle port (oracle/pf_oracle.cpp, -O2, 1 thread): 1 sequence, 4-token prompt, "
-                          f"{steps} decode steps, {gen} tokens in {el:.1f} s on the full 1B model"}
+                "sample": f"oracle port (oracle/pf_oracle.cpp, -O2, 1 thread): 1 sequence of the config at context "
+                          f"{prompt_len} (its {prompt_len}-token prompt prefilled untimed on {host} host threads in "
+                          f"{t_pre:.0f} s), {steps} decode steps, {gen} tokens in {el:.1f} s on the full 1B model"}
     finally:
         L.po_engine_destroy(e)
 
@@ -380,7 +388,7 @@ def main():
     clocks = clk.summary()
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(model)
+        cpu = cpu_baseline(model, min(plen, 512))  # (longer prompts: the first 512 tokens of the context)
     if rank == 0:
         line = {
             "metric": METRIC, "value": tokens_all / (ms_max * 1e-3), "unit": UNIT, "n_gpus": world,

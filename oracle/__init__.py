@@ -143,6 +143,7 @@ def lib():
         _sig(L, "po_engine_probe_row", None, vp, i32, i32, _f32p, _f32p)
         _sig(L, "po_engine_load_synthetic", None, vp, u32, u32, C.c_int)
         _sig(L, "po_engine_set_threads", None, vp, C.c_int)
+        _sig(L, "po_engine_set_prefill_threads", None, vp, C.c_int)
         _lib = L
     return _lib
 

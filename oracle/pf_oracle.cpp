@@ -85,16 +85,34 @@ static void unpack_ternary(const uint8_t* src, int8_t* dst, uint64_t n) {
 // ---------------------------------------------------------------------------
 // A3/A4: matmul_int8, matmul_quantized (src/matmul_neon.cpp:80-181)
 // ---------------------------------------------------------------------------
+// Host threads the output columns of mm_int8 are split over (the engine's
+// prefill sets it; every element is computed the same way on any thread).
+static thread_local int tl_mm_threads = 1;
+
 static void mm_int8(const int8_t* A, const int8_t* B, int32_t* C, uint32_t M, uint32_t N,
                     uint32_t K) {
-    for (uint32_t i = 0; i < M; i++)
-        for (uint32_t j = 0; j < N; j++) {
-            const int8_t* a = A + (size_t)i * K;
-            const int8_t* b = B + (size_t)j * K;
-            int32_t acc = 0;
-            for (uint32_t k = 0; k < K; k++) acc += (int32_t)a[k] * (int32_t)b[k];
-            C[(size_t)i * N + j] = acc;
-        }
+    auto cols = [&](uint32_t j0, uint32_t j1) {
+        for (uint32_t i = 0; i < M; i++)
+            for (uint32_t j = j0; j < j1; j++) {
+                const int8_t* a = A + (size_t)i * K;
+                const int8_t* b = B + (size_t)j * K;
+                int32_t acc = 0;
+                for (uint32_t k = 0; k < K; k++) acc += (int32_t)a[k] * (int32_t)b[k];
+                C[(size_t)i * N + j] = acc;
+            }
+    };
+    const int nt = tl_mm_threads;
+    if (nt <= 1 || (uint64_t)M * N * K < (1u << 20)) {
+        cols(0, N);
+        return;
+    }
+    std::vector<std::thread> pool;
+    const uint32_t per = (N + nt - 1) / nt;
+    for (int t = 0; t < nt; t++) {
+        const uint32_t j0 = t * per, j1 = std::min(N, j0 + per);
+        if (j0 < j1) pool.emplace_back(cols, j0, j1);
+    }
+    for (auto& th : pool) th.join();
 }
 
 static void mm_quant(const float* A, const int8_t* B, float* C, uint32_t M, uint32_t N, uint32_t K,
@@ -798,6 +816,7 @@ struct Engine {
     std::vector<Seq> seqs;
     std::vector<float> last_logits;  // [n_seqs*(K+1)][V]
     int threads = 1;                 // host threads over sequences (prefill, step)
+    int prefill_threads = 1;         // > 1: prefill one sequence at a time, its matmuls on this many threads
 
     int64_t ffn_computed() const {
         int64_t n = 0;
@@ -951,7 +970,8 @@ struct Engine {
         seqs.clear();
         seqs.resize(n);
         const bool greedy = sampling_is_greedy(samp);
-        for_each_seq(n, threads, [&](int b) {
+        for_each_seq(n, prefill_threads > 1 ? 1 : threads, [&](int b) {
+            tl_mm_threads = prefill_threads;
             std::vector<float> lg(V());
             Seq& s = seqs[b];
             new_seq(s, seeds ? seeds[b] : 0u);
@@ -963,6 +983,7 @@ struct Engine {
             }
             s.pending = greedy ? argmax(lg.data(), V()) : sample(lg.data(), V(), samp, draw(s));
             draft(s);
+            tl_mm_threads = 1;
         });
         last_logits.assign((size_t)n * (K() + 1) * V(), 0.0f);
     }
@@ -1241,6 +1262,11 @@ void po_engine_read_skip_counts(void* ep, int64_t* comp, int64_t* skip) {
 // Host threads over sequences for prefill and step (1: one after another;
 // the results do not depend on it).
 void po_engine_set_threads(void* ep, int threads) { ((po::Engine*)ep)->threads = std::max(1, threads); }
+// > 1: prefill sequences one after another with their matmuls' output columns
+// on this many host threads (results do not depend on it).
+void po_engine_set_prefill_threads(void* ep, int threads) {
+    ((po::Engine*)ep)->prefill_threads = std::max(1, threads);
+}
 uint32_t po_engine_read_kv(void* ep, int32_t b, uint32_t l, uint32_t h, int8_t* k, float* ks, int8_t* v,
                            float* vs, uint32_t max_n) {
     auto* e = (po::Engine*)ep;
