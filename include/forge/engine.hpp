@@ -6,9 +6,18 @@
 // heads come from the seeded generator.  generate / forward run the
 // speculative-decode step of forge::BatchEngine: verification of the K MTP
 // drafts in one batched forward, commit of the accepted prefix only, and
-// positions equal to token positions.  The reference's literal Engine
-// (sequential verification, placeholder projections, layer index as the
-// position) is not reproduced.  The device engine supports head_dim 64.
+// positions equal to token positions.  The device engine supports head_dim 64.
+//
+// Reference-compat mode (set_reference_compat(true) before load_model, or
+// FORGE_REFERENCE_COMPAT=1 in the environment when the Engine is constructed)
+// reproduces the reference's literal Engine instead (src/engine.cpp:47-396,
+// 459-854): placeholder projections (the file's layer matrices are never
+// loaded), the layer index as RoPE and KV position with theta 5e6, each K head
+// rotated once per query head, head outputs as the reference leaves them,
+// sequential verification of sampled drafts with no KV rollback, the process-wide
+// sampler, MTP weights drawn from rand() (twice, as the reference's load does)
+// and its memory statistics.  Its forward runs on the device with the
+// reference's float operation order; it needs n_vocab <= 16384 and n_embd <= 4096.
 #ifndef FORGE_B200_ENGINE_HPP
 #define FORGE_B200_ENGINE_HPP
 
@@ -35,6 +44,10 @@ public:
     Engine& operator=(const Engine&) = delete;
 
     bool load_model(const std::string& squeeze_path);
+
+    // Reference-compat mode (see above); takes effect at the next load_model.
+    void set_reference_compat(bool on);
+    bool reference_compat() const { return compat_; }
 
     void set_max_context(uint32_t tokens);
     void set_mtp_enabled(bool enabled);
@@ -74,7 +87,14 @@ public:
     const std::string& last_error() const { return err_; }
 
 private:
+    struct Literal;  // the reference-compat engine (forge/literal.hpp)
     bool ensure_engine();
+    bool compat_load(const std::string& path);
+    GenerationResult compat_generate(const std::vector<int32_t>& prompt, uint32_t max_new, TokenCallback cb,
+                                     ProgressCallback progress);
+    std::vector<float> compat_forward(const std::vector<int32_t>& tokens, std::vector<float>& hidden_out);
+    MemoryStats compat_memory_stats() const;
+    void compat_set_max_context(uint32_t tokens);
     ModelConfig config_;
     std::string path_;
     uint32_t max_context_ = 8192;
@@ -86,6 +106,8 @@ private:
     std::string err_;
     struct Sampler;
     std::unique_ptr<Sampler> sampler_;
+    bool compat_ = false;
+    std::unique_ptr<Literal> lit_;
 };
 
 }  // namespace forge

@@ -207,6 +207,10 @@ def ref():
         _sig(L, "pfref_write_squeeze_model", C.c_int, C.c_char_p, u32, u32, u32, u32, u32, u32, u32, u32, _f32p,
              np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS"))
         _sig(L, "pfref_load_block", C.c_int64, C.c_char_p, u32, u32, _i8p, _f32p, _f32p, C.c_int64)
+        _sig(L, "pfref_write_test_engine_model", C.c_int, C.c_char_p)
+        _sig(L, "pfref_write_literal_model", C.c_int, C.c_char_p, u32, u32, u32, u32, u32, u32, u32, u32, vp, vp,
+             C.c_int)
+        _sig(L, "pfref_literal_script", C.c_int64, C.c_char_p, u32, C.c_uint64, u32, C.c_char_p, C.c_int64)
         _sig(L, "pfref_engine_create", vp)
         _sig(L, "pfref_engine_destroy", None, vp)
         _sig(L, "pfref_seed_sampler", None, u32)

@@ -30,6 +30,7 @@
 #include "forge/layer_skip.hpp"
 #include "forge/matmul_neon.hpp"
 #include "forge/quant_format.hpp"
+#include "literal_script.hpp"
 
 namespace forge {
 void pf_ref_seed_sampler(unsigned s);
@@ -289,6 +290,104 @@ int pfref_literal_generate(const char* path, const int32_t* prompt, uint32_t n, 
     for (size_t i = 0; i < gen; i++) out[i] = r.tokens[n + i];
     *engine_tps = r.tokens_per_second;
     return (int)gen;
+}
+
+// The model of the reference's tests/test_engine.cpp: 2 layers, n_embd 64,
+// 4 / 2 heads, FFN 256, vocabulary 256, max_seq_len 128, 2 MTP heads; Q8
+// layer matrices of uniform [-1, 1] weights after srand(123), no embedding
+// block (so the engine runs its placeholder embedding and logits).
+int pfref_write_test_engine_model(const char* path) {
+    forge::ModelConfig cfg;
+    cfg.n_layers = 2;
+    cfg.n_embd = 64;
+    cfg.n_heads = 4;
+    cfg.n_kv_heads = 2;
+    cfg.n_ff = 256;
+    cfg.n_vocab = 256;
+    cfg.max_seq_len = 128;
+    cfg.mtp_heads = 2;
+    forge::Quantizer q(cfg);
+    std::vector<forge::WeightBlock> blocks;
+    std::vector<std::vector<uint8_t>> data;
+    srand(123);
+    for (uint32_t l = 0; l < cfg.n_layers; l++) {
+        for (uint32_t m = 0; m < 7; m++) {
+            const uint32_t rows = m == 6 ? 256 : 64, cols = (m == 4 || m == 5) ? 256 : 64;
+            std::vector<float> w((size_t)rows * cols);
+            for (auto& x : w) x = ((float)rand() / RAND_MAX) * 2.0f - 1.0f;
+            auto qd = q.quantize_matrix(w.data(), rows, cols, 0);
+            auto comp = q.compress_block(qd);
+            forge::WeightBlock b{};
+            b.layer_id = l;
+            b.matrix_id = m;
+            b.n_rows = rows;
+            b.n_cols = cols;
+            b.compressed_size = (uint32_t)comp.size();
+            b.original_size = (uint32_t)qd.size();
+            b.quant_type = 0;
+            blocks.push_back(b);
+            data.push_back(std::move(comp));
+        }
+    }
+    return q.write_squeeze(path, blocks, data, cfg) ? 0 : -1;
+}
+
+// A model for the literal engine with the blocks it reads: the tied
+// embedding (0, 10) from `emb` (vocab x d floats) and, when `norms` is given,
+// the attention and FFN norm rows (l, 7), (l, 8) and the output norm (0, 9)
+// from norms[(2 * n_layers + 1) x d] (layer-major attention / FFN rows, then
+// the output norm), each quantized by Quantizer::quantize_matrix with `qtype`.
+int pfref_write_literal_model(const char* path, uint32_t n_layers, uint32_t d, uint32_t heads, uint32_t kv_heads,
+                              uint32_t ff, uint32_t vocab, uint32_t max_seq, uint32_t mtp_heads, const float* emb,
+                              const float* norms, int qtype) {
+    forge::ModelConfig c;
+    c.n_layers = n_layers;
+    c.n_embd = d;
+    c.n_heads = heads;
+    c.n_kv_heads = kv_heads;
+    c.n_ff = ff;
+    c.n_vocab = vocab;
+    c.max_seq_len = max_seq;
+    c.mtp_heads = mtp_heads;
+    forge::Quantizer q(c);
+    std::vector<forge::WeightBlock> blocks;
+    std::vector<std::vector<uint8_t>> data;
+    auto add = [&](uint32_t layer, uint32_t m, const float* x, uint32_t rows, uint32_t cols) {
+        auto qd = q.quantize_matrix(x, rows, cols, (uint8_t)qtype);
+        auto comp = q.compress_block(qd);
+        forge::WeightBlock b{};
+        b.layer_id = layer;
+        b.matrix_id = m;
+        b.n_rows = rows;
+        b.n_cols = cols;
+        b.compressed_size = (uint32_t)comp.size();
+        b.original_size = (uint32_t)qd.size();
+        b.quant_type = (uint8_t)qtype;
+        blocks.push_back(b);
+        data.push_back(std::move(comp));
+    };
+    add(0, 10, emb, vocab, d);
+    if (norms) {
+        for (uint32_t l = 0; l < n_layers; l++) {
+            add(l, 7, norms + (size_t)(2 * l) * d, 1, d);
+            add(l, 8, norms + (size_t)(2 * l + 1) * d, 1, d);
+        }
+        add(0, 9, norms + (size_t)(2 * n_layers) * d, 1, d);
+    }
+    return q.write_squeeze(path, blocks, data, c) ? 0 : -1;
+}
+
+// The literal-engine script (oracle/literal_script.hpp) on the reference's
+// Engine, with its sampler reseeded to 42 as at process start.  Returns the
+// transcript length, or -(needed length) when `cap` is too small.
+int64_t pfref_literal_script(const char* path, uint32_t seed, uint64_t max_memory, uint32_t long_tokens, char* out,
+                             int64_t cap) {
+    forge::pf_ref_seed_sampler(42);
+    forge::Engine e;
+    const std::string t = literal_script::run(e, path, seed, (size_t)max_memory, long_tokens);
+    if ((int64_t)t.size() + 1 > cap) return -(int64_t)(t.size() + 1);
+    std::memcpy(out, t.c_str(), t.size() + 1);
+    return (int64_t)t.size();
 }
 
 // ---- Engine sampling (src/engine.cpp:881-1003) ----

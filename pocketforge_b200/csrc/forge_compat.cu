@@ -45,11 +45,12 @@ __global__ void gemv_f32_kernel(const float* __restrict__ x, const float* __rest
 }
 
 // a = silu(g) * u with silu(x) = x / (1 + exp(-x)) (src/mtp.cpp); then the
-// residual h += o is a separate launch after the down projection.
+// residual h += o is a separate launch after the down projection.  The
+// exponential is the double one rounded to float (the correctly rounded value).
 __global__ void silu_mul_kernel(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ a,
                                 uint32_t n) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) a[i] = __fmul_rn(__fdiv_rn(g[i], __fadd_rn(1.0f, expf(-g[i]))), u[i]);
+    if (i < n) a[i] = __fmul_rn(__fdiv_rn(g[i], __fadd_rn(1.0f, (float)exp((double)-g[i]))), u[i]);
 }
 __global__ void vec_add_kernel(float* __restrict__ y, const float* __restrict__ x, uint32_t n) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <cstddef>
+#include <cstdint>
 #include <cstdio>
 
 #include "pf_b200.h"
@@ -78,4 +79,11 @@ inline bool to_host(void* h, const void* d, size_t n, const char* what) {
 }
 
 }  // namespace dev
+
+namespace detail {
+// MTPHeads::quantize_q4 of a rows x cols float matrix (src/mtp.cpp:174-197):
+// per-row scales amax / 127, two values per byte, low nibble first.
+void quantize_q4_rows(const float* src, uint8_t* dst, float* scales, uint32_t rows, uint32_t cols);
+}  // namespace detail
+
 }  // namespace forge

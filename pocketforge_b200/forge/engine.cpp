@@ -4,15 +4,24 @@
 
 #include <chrono>
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 #include <random>
 
 #include "device.hpp"
+#include "literal.hpp"
 #include "squeeze.hpp"
 
 namespace forge {
 
+// One generator for every Engine of the process, as the reference's
+// file-static std::mt19937 rng_engine(42) (src/engine.cpp:16).
+std::mt19937& reference_rng() {
+    static std::mt19937 rng(42);
+    return rng;
+}
+
 struct Engine::Sampler {
-    std::mt19937 rng{42};  // the reference's file-static generator (src/engine.cpp:16)
     dev::Buffer logits, u, out;
 };
 
@@ -20,10 +29,23 @@ size_t Engine::MemoryStats::total() const {
     return weights_mmap + weights_decompressed + kv_cache + activations + prefetch_buffer + mtp_heads + other;
 }
 
-Engine::Engine() : sampler_(new Sampler) {}
+Engine::Engine() : sampler_(new Sampler) {
+    const char* env = std::getenv("FORGE_REFERENCE_COMPAT");
+    compat_ = env && *env && std::strcmp(env, "0") != 0;
+}
 Engine::~Engine() = default;
 
+void Engine::set_reference_compat(bool on) {
+    if (on != compat_) {
+        engine_.reset();
+        lit_.reset();
+        path_.clear();
+    }
+    compat_ = on;
+}
+
 bool Engine::load_model(const std::string& path) {
+    if (compat_) return compat_load(path);
     squeeze::File f;
     if (!f.open(path, &err_)) {
         std::fprintf(stderr, "forge::Engine::load_model: %s\n", err_.c_str());
@@ -70,18 +92,27 @@ bool Engine::ensure_engine() {
 }
 
 void Engine::set_max_context(uint32_t tokens) {
+    if (compat_) return compat_set_max_context(tokens);
     if (tokens != max_context_) engine_.reset();
     max_context_ = tokens;
 }
-void Engine::set_mtp_enabled(bool enabled) { mtp_enabled_ = enabled; }
+void Engine::set_mtp_enabled(bool enabled) {
+    mtp_enabled_ = enabled;
+    config_.mtp_enabled = enabled;
+}
 void Engine::set_layer_skip_threshold(float threshold) {
     skip_threshold_ = threshold;
+    config_.skip_threshold = threshold;
     if (engine_) engine_->set_skip_threshold(threshold);
 }
-void Engine::set_max_memory(size_t bytes) { max_memory_ = bytes; }
+void Engine::set_max_memory(size_t bytes) {
+    max_memory_ = bytes;
+    config_.max_memory = bytes;
+}
 
 GenerationResult Engine::generate(const std::vector<int32_t>& prompt, uint32_t max_new_tokens, TokenCallback callback,
                                   ProgressCallback progress) {
+    if (compat_) return compat_generate(prompt, max_new_tokens, callback, progress);
     GenerationResult r;
     r.tokens = prompt;
     if (prompt.empty() || max_new_tokens == 0 || !ensure_engine()) return r;
@@ -133,6 +164,7 @@ std::vector<float> Engine::forward(const std::vector<int32_t>& tokens) {
 }
 
 std::vector<float> Engine::forward_with_hidden(const std::vector<int32_t>& tokens, std::vector<float>& hidden_out) {
+    if (compat_) return compat_forward(tokens, hidden_out);
     std::vector<float> out;
     if (tokens.empty() || !ensure_engine() || !engine_->prefill({tokens})) return out;
     std::vector<float> lg;
@@ -154,7 +186,7 @@ int32_t Engine::sample(const float* logits, uint32_t n, const SamplingConfig& cf
         if (dev::ok(pf_argmax_rows(dl, 1, (int32_t)n, dout, nullptr), "Engine::sample")) dev::to_host(&tok, dout, 4, "Engine::sample");
         return tok;
     }
-    const float u = std::uniform_real_distribution<float>(0.0f, 1.0f)(s.rng);
+    const float u = std::uniform_real_distribution<float>(0.0f, 1.0f)(reference_rng());
     pf_sampling_config c{cfg.temperature, cfg.top_p, cfg.top_k, 0};
     if (!dev::to_dev(du, &u, 4, "Engine::sample")) return tok;
     if (dev::ok(pf_sample_rows(dl, 1, (int32_t)n, &c, du, dout, nullptr), "Engine::sample"))
@@ -185,6 +217,7 @@ int32_t Engine::sample_top_p(const float* logits, uint32_t n, float p, float tem
 }
 
 Engine::MemoryStats Engine::get_memory_stats() const {
+    if (compat_) return compat_memory_stats();
     MemoryStats m;
     if (!engine_) return m;
     const ModelConfig& c = config_;

@@ -11,7 +11,7 @@
 
 namespace forge {
 
-namespace {
+namespace detail {
 
 // Q4 quantization of an MTP matrix (MTPHeads::quantize_q4, src/mtp.cpp:174-197):
 // per-row scale amax/127; the even element of each pair is scaled by
@@ -38,7 +38,9 @@ void quantize_q4_rows(const float* src, uint8_t* dst, float* scales, uint32_t ro
     }
 }
 
-}  // namespace
+}  // namespace detail
+
+using detail::quantize_q4_rows;
 
 struct MTPHeads::Impl {
     // Per head, device: gate [ff][d/2], up [ff][d/2], down [d][ff/2] packed + scales.
