@@ -239,6 +239,13 @@ PF_API pf_status pf_gemm_packed_static(const int8_t* Aq, const float* a_scale, c
                                        const float* w_scale, int32_t qtype, float* C, int32_t M, int32_t N,
                                        int32_t K, void* stream);
 
+/* Diagnostic with no counterpart in the reference: checks, on the device,
+ * the branch-free correctly rounded reciprocal that the projection kernels'
+ * SwiGLU epilogue uses against CUDA's __frcp_rn for every float in
+ * [1, +inf].  *mismatches receives the count, *first_bad the lowest
+ * mismatching bit pattern (0xFFFFFFFF if none). */
+PF_API pf_status pf_check_reciprocal(uint64_t* mismatches, uint32_t* first_bad);
+
 /* ------------------------------------------------------------------ */
 /* Engine: batched MTP speculative decoding                             */
 /* (Engine::generate / forward_with_hidden / MTPHeads::forward,         */

@@ -11,12 +11,18 @@
 //   warps 2..9: unpack the weight block into unpacked-weight buffer b
 //     (= stage % 2) in the tensor core's K-major 128-byte-swizzled layout
 //     (the layout the TMA produces for the activations), each weight in the
-//     top bits of its byte; fence the generic->async proxy; arrive on
-//     b_full[b];
+//     top bits of its byte; fence the generic->async proxy; one arrival per
+//     warp on b_full[b] (256 single-thread arrivals on one barrier word
+//     serialised the hand-off);
 //   warp 1, one thread: four tcgen05.mma (K = 32 each) per activation plane
 //     into TMEM, then tcgen05.commit -> empty[s] and b_empty[b].
-// The load ring has more slots than the two unpacked buffers, so more copies
-// are in flight per shared-memory byte.
+// The K loop is bound by shared-memory bandwidth: per stage the TMA writes,
+// the unpack's loads and stores and the tensor core's operand reads (at
+// BN = 256, 128 KB, ~0.5 us at 128 B per clock).  Loading the packed weights
+// into registers instead of through the TMA saved nothing (global loads fill
+// the same on-chip array) and lengthened the K loop.  The load ring has more
+// slots than the two unpacked buffers, so more copies are in flight per
+// shared-memory byte.
 // After the last stage a commit on `done` releases warps 2..9 to read the
 // accumulators (tcgen05.ld 32x32b: warp w reads TMEM lanes 32*(w%4)..+31,
 // i.e. output rows, and one half of the columns), shift the sums back to the
@@ -40,6 +46,7 @@
 
 #include "gemm.cuh"
 #include "gemm_tc.cuh"
+#include "numerics.cuh"
 
 namespace pf {
 
@@ -116,13 +123,24 @@ __device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+// 16 columns of this warp's 32 TMEM lanes; the registers are valid only
+// after tmem_wait_ld().
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    tmem_ld16_nowait(taddr, r);
+    tmem_wait_ld();
+}
+// The tensor maps live in kernel parameter space; fetching them ahead of the
+// first copy takes the descriptor fetch off that copy's latency.
+__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
 // Barrier of the epilogue warps only (named barrier 1).
@@ -188,10 +206,7 @@ __device__ __forceinline__ float col_value(const int32_t (&a)[P], float a_s, flo
     }
 }
 
-__device__ __forceinline__ float engine_swiglu(float g, float u) {  // engine FFN form
-    const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
-    return __fmul_rn(__fmul_rn(g, sig), u);
-}
+__device__ __forceinline__ float engine_swiglu(float g, float u) { return engine_swiglu_rn(g, u); }  // engine FFN form
 __device__ __forceinline__ float mtp_swiglu(float g, float u) {  // MTP head FFN form
     return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
 }
@@ -203,15 +218,17 @@ __device__ __forceinline__ void rope_pair(float& x0, float& x1, float c, float s
     x1 = r1;
 }
 
-// Pass 2 of the epilogue: one warp writes its 32 staged rows.  Lane l owns
-// columns 4*(l % CPR) .. +3 of row l / CPR of each group, so every store
-// (and every residual load) is a contiguous run of a row.  Row-dependent
-// inputs (residual rows, RoPE angles) are fetched for U groups before any of
-// them is written, keeping several loads in flight.
-template <int BN, int EPI>
+// Pass 2 of the epilogue: one warp writes its 32 staged rows of BN values
+// (row stride SROW floats).  Lane l owns columns 4*(l % CPR) .. +3 of row
+// l / CPR of each group, so every store (and every residual load) is a
+// contiguous run of a row.  Row-dependent inputs (residual rows, RoPE angles)
+// are fetched for U groups before any of them is written, keeping several
+// loads in flight.  The SwiGLU forms stage their outputs (pass 1 applies the
+// activation), so for them BN counts output columns and n0 is an output
+// column.
+template <int BN, int SROW, int EPI>
 __device__ __forceinline__ void store_rows(const GemmParams& p, const float* stg, int rbase, int n0, int lane,
                                            int32_t* out_i32) {
-    constexpr int SROW = BN + 4;
     constexpr int CPR = BN / 4, RPI = 32 / CPR, ITERS = 32 / RPI, U = 4;
     static_assert(ITERS % U == 0, "row groups");
     const int cg = lane % CPR, ro = lane / CPR;
@@ -265,12 +282,8 @@ __device__ __forceinline__ void store_rows(const GemmParams& p, const float* stg
                 r.z = __fadd_rn(r.z, x.z);
                 r.w = __fadd_rn(r.w, x.w);
                 *reinterpret_cast<float4*>(p.resid + (size_t)m * p.ldo + n) = r;
-            } else if constexpr (EPI == EPI_SWIGLU) {
-                *reinterpret_cast<float2*>(p.out + (size_t)m * p.ldo + (n >> 1)) =
-                    make_float2(engine_swiglu(x.x, x.y), engine_swiglu(x.z, x.w));
-            } else if constexpr (EPI == EPI_MTP_SWIGLU3) {
-                *reinterpret_cast<float2*>(p.out + (size_t)m * p.ldo + (n >> 1)) =
-                    make_float2(mtp_swiglu(x.x, x.y), mtp_swiglu(x.z, x.w));
+            } else if constexpr (EPI == EPI_SWIGLU || EPI == EPI_MTP_SWIGLU3) {
+                *reinterpret_cast<float4*>(p.out + (size_t)m * p.ldo + n) = x;  // activations of pass 1
             }
         }
     }
@@ -305,6 +318,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // The next kernel may start its prologue now; it waits for this grid's
     // completion before it reads anything this grid writes.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (threadIdx.x == 0) {
+        prefetch_map(&tmA);
+        prefetch_map(&tmB);
+    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
     const int nkt = p.K / BK;
@@ -318,7 +335,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mbar_init(empty(s), 1);
         }
         for (int b = 0; b < NB; b++) {
-            mbar_init(b_full(b), NUM_UNPACK);
+            mbar_init(b_full(b), NUM_UNPACK / 32);  // one arrival per unpack warp
             mbar_init(b_empty(b), 1);
         }
         mbar_init(done, 1);
@@ -379,7 +396,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             constexpr uint32_t idesc = idesc_i8(BN);
             for (int i = 0; i < nst && !*abort_flag; i++) {
                 const int s = i % STAGES, ph = (i / STAGES) & 1;
-                // b_full completes only after every unpack thread saw
+                // b_full completes only after every unpack warp saw
                 // full_raw (activation and weight copies landed) and
                 // arrived, so it orders the MMAs after both.
                 const int b = i % NB;
@@ -410,10 +427,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         constexpr int CH_IN = BN * RB / 16;  // 16-byte packed chunks per stage
         constexpr int PER = (CH_IN + NUM_UNPACK - 1) / NUM_UNPACK;
         static_assert(CH_IN % NUM_UNPACK == 0 || PER == 1, "partial rounds only with one chunk per thread");
-        for (int i = 0; i < nst && !*abort_flag; i++) {
+        for (int i = 0; i < nst; i++) {
+            // Exits are warp-uniform: the warp arrives on b_full as one below.
+            if (__shfl_sync(0xffffffffu, *abort_flag, 0)) break;
             const int s = i % STAGES, ph = (i / STAGES) & 1;
             const int b = i % NB;
-            if (!mbar_wait(full_raw(s), ph) || !mbar_wait(b_empty(b), ((i / NB) & 1) ^ 1)) {
+            const bool got = mbar_wait(full_raw(s), ph) && mbar_wait(b_empty(b), ((i / NB) & 1) ^ 1);
+            if (!__all_sync(0xffffffffu, got)) {
                 fail();
                 break;
             }
@@ -451,8 +471,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     *reinterpret_cast<uint4*>(rb + ((c ^ r7) << 4)) = w;
                 }
             }
+            // Every thread makes its generic-proxy writes visible to the
+            // tensor core's async proxy; the warp then arrives once.
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_arrive(b_full(b));
+            __syncwarp();
+            if (lane == 0) mbar_arrive(b_full(b));
         }
         // ---------------- epilogue ----------------
         asm volatile("griddepcontrol.wait;" ::: "memory");  // resid, scales, workspace of earlier kernels
@@ -510,32 +533,58 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             float* stg = reinterpret_cast<float*>(smem) + (warp - 2) * 32 * Ly::SROW;
             const float a_s = (in_m && EPI != EPI_I32) ? p.a_scale[m] : 0.0f;  // (int32 slices: no scales)
             const float s_all = __fmul_rn(a_s, p.w_scale_all);
-            for (int j = 0; j < HALF / 16; j++) {
-                uint32_t r[P][16];
+            constexpr bool SWI = EPI == EPI_SWIGLU || EPI == EPI_MTP_SWIGLU3;
+            // TMEM chunks loaded per wait: one round trip covers up to 64 columns.
+            constexpr int JB = (P == 1) ? (HALF / 16 < 4 ? HALF / 16 : 4) : 1;
+            static_assert((HALF / 16) % JB == 0, "chunk batches");
+            for (int j0 = 0; j0 < HALF / 16; j0 += JB) {
+                uint32_t r[JB][P][16];
                 if (p.splits > 1 && p.slice_stride == 0) {
                     // All loads of the chunk are issued before anything is
                     // written; the workspace is re-zeroed after the tile.
 #pragma unroll
-                    for (int pl = 0; pl < P; pl++)
+                    for (int jj = 0; jj < JB; jj++)
 #pragma unroll
-                        for (int c = 0; c < 16; c++)
-                            r[pl][c] = in_m ? (uint32_t)__ldcg(p.ws + ((size_t)pl * p.N + n0 + c0 + j * 16 + c) * p.M + m)
-                                            : 0u;
+                        for (int pl = 0; pl < P; pl++)
+#pragma unroll
+                            for (int c = 0; c < 16; c++)
+                                r[jj][pl][c] =
+                                    in_m ? (uint32_t)__ldcg(p.ws + ((size_t)pl * p.N + n0 + c0 + (j0 + jj) * 16 + c) * p.M + m)
+                                         : 0u;
                 } else {
 #pragma unroll
-                    for (int pl = 0; pl < P; pl++) tmem_ld16(tbase + (uint32_t)(pl * BN + c0 + j * 16), r[pl]);
+                    for (int jj = 0; jj < JB; jj++)
+#pragma unroll
+                        for (int pl = 0; pl < P; pl++)
+                            tmem_ld16_nowait(tbase + (uint32_t)(pl * BN + c0 + (j0 + jj) * 16), r[jj][pl]);
+                    tmem_wait_ld();
                 }
-                float v[16];
 #pragma unroll
-                for (int c = 0; c < 16; c++) {
-                    int32_t a[P];
+                for (int jj = 0; jj < JB; jj++) {
+                    const int j = j0 + jj;
+                    float v[16];
 #pragma unroll
-                    for (int pl = 0; pl < P; pl++) a[pl] = (int32_t)r[pl][c] >> SHIFT;  // exact: a multiple of 2^SHIFT
-                    v[c] = col_value<P, EPI>(a, a_s, s_wsc[c0 + j * 16 + c], s_all);
+                    for (int c = 0; c < 16; c++) {
+                        int32_t a[P];
+#pragma unroll
+                        for (int pl = 0; pl < P; pl++) a[pl] = (int32_t)r[jj][pl][c] >> SHIFT;  // exact: a multiple of 2^SHIFT
+                        v[c] = col_value<P, EPI>(a, a_s, s_wsc[c0 + j * 16 + c], s_all);
+                    }
+                    if constexpr (SWI) {
+                        // (gate, up) column pairs -> 8 activations of this row
+                        float o[8];
+#pragma unroll
+                        for (int q = 0; q < 8; q++)
+                            o[q] = EPI == EPI_SWIGLU ? engine_swiglu(v[2 * q], v[2 * q + 1]) : mtp_swiglu(v[2 * q], v[2 * q + 1]);
+                        float4* d = reinterpret_cast<float4*>(stg + lane * Ly::SROW + j * 8);
+                        d[0] = make_float4(o[0], o[1], o[2], o[3]);
+                        d[1] = make_float4(o[4], o[5], o[6], o[7]);
+                    } else {
+                        float4* d = reinterpret_cast<float4*>(stg + lane * Ly::SROW + j * 16);
+#pragma unroll
+                        for (int q = 0; q < 4; q++) d[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                    }
                 }
-                float4* d = reinterpret_cast<float4*>(stg + lane * Ly::SROW + j * 16);
-#pragma unroll
-                for (int q = 0; q < 4; q++) d[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
             }
             __syncwarp();
             if (p.splits > 1 && p.slice_stride == 0 && in_m) {
@@ -545,7 +594,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             // Pass 2: whole rows, 4 adjacent columns per lane, coalesced.
             // Slices mode: split z writes its own int32 tile (reduced later).
             int32_t* oi = p.out_i32 ? p.out_i32 + (size_t)blockIdx.z * p.slice_stride : nullptr;
-            store_rows<HALF, EPI>(p, stg, m0 + sub * 32, n0 + c0, lane, oi);
+            if constexpr (SWI)
+                store_rows<HALF / 2, Ly::SROW, EPI>(p, stg, m0 + sub * 32, (n0 + c0) >> 1, lane, oi);
+            else
+                store_rows<HALF, Ly::SROW, EPI>(p, stg, m0 + sub * 32, n0 + c0, lane, oi);
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;");

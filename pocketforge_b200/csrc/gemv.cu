@@ -29,6 +29,7 @@
 #include <algorithm>
 
 #include "gemm.cuh"
+#include "numerics.cuh"
 #include "gemm_tc.cuh"
 
 namespace pf {
@@ -52,10 +53,7 @@ struct Fmt {
 
 __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
 
-__device__ __forceinline__ float engine_swiglu(float g, float u) {  // engine FFN form (gemm_tc.cu)
-    const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
-    return __fmul_rn(__fmul_rn(g, sig), u);
-}
+__device__ __forceinline__ float engine_swiglu(float g, float u) { return engine_swiglu_rn(g, u); }  // engine FFN form
 
 // acc[r] += dot(activation row r over this chunk's K values, weights w)
 template <int WF, int RT>

@@ -287,3 +287,13 @@ def test_empty_batches_are_noops():
     torch.cuda.synchronize()
     assert L.pf_matmul_int8(p(i8), p(i8), p(i32), 4, 0, 128, None) == 1  # N = 0: PF_ERR_INVALID
     assert L.pf_gemm_packed(p(i8), p(f), p(packed), p(f), 1, p(f), 4, 64, 100, None) == 1  # K % 128 != 0
+
+
+def test_branch_free_reciprocal_is_correctly_rounded():
+    """The SwiGLU epilogues take 1 / (1 + exp(-g)) from a branch-free double
+    Newton iteration (numerics.cuh) so that many of them interleave; it must
+    equal the correctly rounded reciprocal (CUDA's __frcp_rn) for every float
+    in [1, +inf], which the device checks exhaustively."""
+    bad, first = C.c_uint64(0), C.c_uint32(0)
+    _lib.check(_lib.lib().pf_check_reciprocal(C.byref(bad), C.byref(first)), "pf_check_reciprocal")
+    assert bad.value == 0, f"{bad.value} mismatches, first at bits {first.value:#010x}"
