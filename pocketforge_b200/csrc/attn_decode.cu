@@ -4,27 +4,36 @@
 // Same semantics as attention() in attention.cu (KVCache::attention_scores /
 // attention_weighted_sum + Engine::compute_attention, src/kv_cache.cpp:129-198,
 // src/engine.cpp:753-779).  Every int8 entry a row can see goes through
-// tensor-core MMAs, 32 entries (one block) at a time:
-//   scores  S = Q . K^T : Q (fp32 after RoPE) split into three int8 digit
+// tensor-core MMAs, 32 entries (one block) at a time, with the entries as the
+// MMAs' M dimension and the query rows as N (8-row tiles: 20 rows of a
+// K = 4 verify batch pad to 24, not to 32):
+//   scores  S^T = K . Q^T : Q (fp32 after RoPE) split into three int8 digit
 //           planes per row (x = s(q1 + q2/254 + q3/254^2)), K the stored int8,
 //           mma.sync m16n8k32.s8: the int32 products are exact and are
 //           recombined in fp32 (~1e-7 relative, unbiased);
 //           s_raw = S * k_scale, and the score in log2 units is f * s_raw with
 //           f = s * log2(e) / sqrt(64).
-//   output  O = W . V   : w = p * v_scale / 2^E (E = a power-of-two reference
-//           for the v scales, per warp) split into two fp16 planes, w = hi +
-//           lo (hi truncated to 11 significant bits, lo the fp16-rounded
-//           remainder: ~22 bits), V the stored int8, exact in fp16;
-//           mma.sync m16n8k16 with fp32 accumulators.  Each block's products
-//           start from a zero accumulator (the small plane first) and are added
-//           to the running sums with a rounded fp32 add, so the tensor cores'
-//           accumulation rounding does not build up over the context.
+//   output  O^T = V^T . W^T : w = p * v_scale / 2^E (E = a power-of-two
+//           reference for the v scales, per warp) split into two fp16 planes,
+//           w = hi + lo (hi truncated to 11 significant bits, lo the
+//           fp16-rounded remainder: ~22 bits), V the stored int8, exact in
+//           fp16; mma.sync m16n8k16 with fp32 accumulators.  The score
+//           accumulator of a thread (entry e, rows 2t, 2t+1) is one row of an
+//           8 x 8 fp16 tile; movmatrix.trans turns it into the B fragment of
+//           the value MMA.  Each block's products start from a zero
+//           accumulator (the small plane first) and are added to the running
+//           sums with a rounded fp32 add, so the tensor cores' accumulation
+//           rounding does not build up over the context.
 // Online softmax per row with a lazily raised maximum: the reference point
 // moves only when a block's maximum exceeds it by more than 8 (log2 units),
 // so p = 2^((s_raw - m) f) stays <= 2^8 and the fp16 planes stay in range.
-// Maxima stay in the raw units of the scores, and every exponent is an exact
-// difference of two raw scores times f (as exp(s - max) in the reference):
-// a product f * m, rounded, would cost an ulp of a large number.
+// A thread checks its own entries; only when some thread sees a score past
+// the limit does the warp reduce the rows' maxima (shuffles over the 8
+// threads sharing a row).  The row sums are per-thread partial sums, reduced
+// once at the end.  Maxima stay in the raw units of the scores, and every
+// exponent is an exact difference of two raw scores times f (as exp(s - max)
+// in the reference): a product f * m, rounded, would cost an ulp of a large
+// number.
 //
 // Blocks are the committed pool blocks, the window-ring blocks, and one extra
 // block assembled in shared memory from the sink entries, the pool entries
@@ -33,21 +42,26 @@
 // row is added when the partial softmax states are merged.
 //
 // Grid (sequence, kv head, split).  A split takes a contiguous range of the
-// (sequence, kv head)'s blocks; its four warps take the blocks of the range in
-// turn, each with all query rows (MT m-tiles of 16) and its own cp.async ring,
-// so the block loop has no CTA-wide barrier.  The warps' states are merged in
-// shared memory; with more than one split each split writes its state to a
-// workspace and the last split to arrive (a counter per (sequence, kv head),
-// reset by that split) merges them, adds the self term and writes the output.
+// (sequence, kv head)'s blocks; its three warps take the blocks of the range
+// in turn, each with all query rows (NT tiles of 8) and its own cp.async
+// ring, so the block loop has no CTA-wide barrier.  Three warps and 168
+// registers a thread let four CTAs share an SM, so the 512 (sequence, kv
+// head) units of a 64-sequence batch run as one wave (with four warps per
+// CTA, three CTAs fit and the last 68 units formed a second wave that took
+// ~40% of the launch).  The warps' states are merged in shared memory; with
+// more than one split each split writes its state to a workspace and the last
+// split to arrive (a counter per (sequence, kv head), reset by that split)
+// merges them, adds the self term and writes the output.
 //
 // Fragment layouts: the k index of an MMA can be any permutation of the
 // reduced dimension as long as A and B agree.
-//   QK (m16n8k32): thread (g, t) uses bytes [16t, 16t+16) of K row g and of Q
-//       rows g, g+8; k-step 0 takes bytes 0-7, k-step 1 bytes 8-15.
-//   PV (m16n8k16): the QK accumulator of thread (g, t) holds entries 8j + 2t + {0,1}
-//       (j = n8 tile); tiles 2s, 2s+1 are the A fragment of k-step s, and V is
-//       stored dim-major per 32-entry block in the matching entry order
-//       (kv_vpos in kv.cuh): one 8-byte load per dim row gives both k-steps.
+//   QK (m16n8k32): thread (g, t) uses bytes [16t, 16t+16) of K rows g, g+8
+//       (A) and of query row g of the tile (B); k-step 0 takes bytes 0-7,
+//       k-step 1 bytes 8-15, so the digit planes are stored in natural order.
+//   PV (m16n8k16): A = V^T, thread (g, t) needs entries 16 ks + {2t, 2t+1,
+//       2t+8, 2t+9} of dims g, g+8; V is stored dim-major per 32-entry block
+//       in that entry order (kv_vpos in kv.cuh): one 8-byte load per dim row
+//       gives both k-steps.
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -59,9 +73,11 @@ namespace pf {
 
 namespace {
 
-constexpr int QR = 32;   // padded query rows per CTA
-constexpr int NW = 4;    // warps per CTA
-constexpr int NSW = 3;   // cp.async stages per warp
+constexpr int QR = 32;   // query rows per CTA at most
+constexpr int ACC_STRIDE = 68;  // floats per row of the warps' merge sums
+constexpr int NW = 3;    // warps per CTA (3: four CTAs fit an SM, one wave for 512 units)
+constexpr int NT_THREADS = 32 * NW;
+constexpr int NSW = 3;   // cp.async stages per warp (two blocks of lookahead)
 constexpr int BIG = 1 << 30;
 constexpr int PART = 68; // floats per (split, row) partial state: m, l, pad, pad, o[64]
 constexpr int kMaxSplits = 8;  // context splits per (sequence, kv head, row group)
@@ -69,9 +85,11 @@ constexpr int NEXMAX = 4; // extra blocks (sinks, in-batch pool entries, earlier
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kMaxLead = 8.0f;  // log2 units a block max may exceed the reference before it moves
 
+// The MMAs below are plain (non-volatile) asm: they only read and write
+// registers, so the compiler may interleave independent accumulator chains.
 __device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                         uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};\n"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
@@ -80,7 +98,7 @@ __device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1,
 
 __device__ __forceinline__ void mma_s8(int32_t (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                        uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};\n"
         : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
@@ -130,6 +148,13 @@ __device__ __forceinline__ uint32_t pack_h2(float lo_half, float hi_half) {
     const __half2 h = __floats2half2_rn(lo_half, hi_half);
     return *reinterpret_cast<const uint32_t*>(&h);
 }
+// Transpose of an 8 x 8 tile of 16-bit values held one row pair per thread
+// (thread (g, t): row g, columns 2t, 2t + 1).
+__device__ __forceinline__ uint32_t movm_trans(uint32_t x) {
+    uint32_t y;
+    asm("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
 // x = hi + lo: hi keeps 11 significant bits (exact in fp16 for |x| >= 2^-14).
 __device__ __forceinline__ float trunc11(float x) { return __int_as_float(__float_as_int(x) & (int)0xFFFFE000u); }
 
@@ -143,14 +168,6 @@ __device__ __forceinline__ float pow2i(int k) { return __int_as_float((127 + k) 
 // Exponent e with x in [2^(e-1), 2^e), for finite x > 0.
 __device__ __forceinline__ int exp_of(float x) { return ((__float_as_int(x) >> 23) & 0xFF) - 126; }
 
-__device__ __forceinline__ float quad_max(float v) {
-    v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
-    return fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
-}
-__device__ __forceinline__ float quad_sum(float v) {
-    v += __shfl_xor_sync(0xffffffffu, v, 1);
-    return v + __shfl_xor_sync(0xffffffffu, v, 2);
-}
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -179,19 +196,18 @@ struct __align__(16) BlockBuf {
     float ks[32], vs[32];
 };
 
-template <int MT, int NEX>
+template <int NT, int NEX>
 struct __align__(16) AttnSmem {
-    uint4 qf[MT][3][2][32];  // query digit planes as A fragments [m-tile][plane][k-step][lane]
+    int8_t qd[3][8 * NT][64];  // query digit planes [plane][row][dim] (B fragments of the score MMA)
     float fr[QR];            // per row: f = s * log2(e) / 8 (0 for padding rows)
     float s_self[QR];        // self-term score, raw units
-    float v_self[QR][64];    // self-term values
     BlockBuf ex[NEX];        // the extra blocks
     int ex_lo[32 * NEX], ex_hi[32 * NEX];  // rows of the sequence that see each extra entry
     union {
         BlockBuf ring[NW][NSW];
         struct {
             float m[NW][QR], l[NW][QR];  // raw-unit maxima, sums
-            float acc[NW][QR][64];       // true-scale weighted sums
+            float acc[NW][QR][ACC_STRIDE];  // true-scale weighted sums (padded rows: no bank conflicts)
         } merge;
     } u;
     float cm[QR], cl[QR];    // the CTA's merged state (with acc in u.merge.acc[0])
@@ -200,13 +216,14 @@ struct __align__(16) AttnSmem {
 
 }  // namespace
 
-template <int MT, int NEX>
-__global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int layer, RowBatch rb, const float* __restrict__ qkv,
+template <int NT, int NEX>
+__global__ void __launch_bounds__(NT_THREADS, NT <= 3 ? 4 : 2) attn_decode_kernel(KvCache kv, int layer, RowBatch rb, const float* __restrict__ qkv,
                                                           int ld, int k_col, int v_col, int H, Staged st, SpecPool sp,
                                                           AttnWork aw, int nsplit, float* __restrict__ out, int ldo,
                                                           uint32_t* err) {
     extern __shared__ __align__(16) uint8_t attn_smem_raw[];
-    AttnSmem<MT, NEX>& sm = *reinterpret_cast<AttnSmem<MT, NEX>*>(attn_smem_raw);
+    AttnSmem<NT, NEX>& sm = *reinterpret_cast<AttnSmem<NT, NEX>*>(attn_smem_raw);
+    constexpr int QP = 8 * NT;  // query rows padded to whole 8-row tiles
     const int b = blockIdx.x, g = blockIdx.y;
     const int split = (int)blockIdx.z % nsplit, rg = (int)blockIdx.z / nsplit;
     const int n = rb.n[b];
@@ -221,7 +238,7 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
     }
     const int nr = min(rpc, n - r0);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
-    const int rows = qpk * nr;  // <= 16 * MT (checked on the host)
+    const int rows = qpk * nr;  // <= QP (checked on the host)
     const int L0 = rb.len0[b], row0 = rb.row0[b];
     const int plast = L0 + n - 1;
     const int cs = min(L0, kv.S);
@@ -235,7 +252,7 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
     // earlier rows of the batch: row r sees staged rows j < r, and this CTA's
     // last row is r0 + nr - 1
     const int n_ex = cs + n_spec + (r0 + nr - 1);
-    if (n_ex > 32 * NEX || rows > 16 * MT) {  // excluded by the host; never index past the tiles
+    if (n_ex > 32 * NEX || rows > QP) {  // excluded by the host; never index past the tiles
         if (tid == 0 && err) atomicOr(err, ERR_BOUNDS);
         asm volatile("griddepcontrol.wait;" ::: "memory");
         return;
@@ -309,19 +326,22 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
     };
     // this split owns some extra block: it assembles all of them
     const bool own_ex = nex > 0 && b_end > nkv && b_begin < nblk;
-    // task t (< nex * 128): entry t >> 2, dims [16*(t&3), +16)
-    uint4 ex_k[NEX], ex_v[NEX];
-    float ex_ks[NEX], ex_vs[NEX];
-    int ex_lo[NEX];
+    // task t (< nex * 128, strided over the CTA's threads): entry t >> 2,
+    // dims [16*(t&3), +16)
+    constexpr int EXT = (128 * NEX + NT_THREADS - 1) / NT_THREADS;  // tasks per thread
+    uint4 ex_k[EXT], ex_v[EXT];
+    float ex_ks[EXT], ex_vs[EXT];
+    int ex_lo[EXT];
 #pragma unroll
-    for (int x = 0; x < NEX; x++) {
-        const int e = (tid + 128 * x) >> 2, q4 = tid & 3;
+    for (int x = 0; x < EXT; x++) {
+        const int task = tid + NT_THREADS * x;
+        const int e = task >> 2, q4 = task & 3;
         ex_k[x] = make_uint4(0, 0, 0, 0);
         ex_v[x] = make_uint4(0, 0, 0, 0);
         ex_ks[x] = 0.0f;
         ex_vs[x] = 0.0f;
         ex_lo[x] = BIG;
-        if (own_ex && e < n_ex) {
+        if (own_ex && task < 128 * NEX && e < n_ex) {
             const int8_t *kp, *vp;
             const float *ksp, *vsp;
             ex_src(e, kp, vp, ksp, vsp, ex_lo[x]);
@@ -332,9 +352,9 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
         }
     }
 
-    // ---- queries -> fp16 fragment planes; self-term score and value ----
-    constexpr int RPW = 4 * MT;  // query rows per warp: warp + NW * k
-    float qx[RPW][2], kx[RPW][2], vx[RPW][2];
+    // ---- queries -> int8 digit planes; self-term score ----
+    constexpr int RPW = (QP + NW - 1) / NW;  // query rows per warp: warp + NW * k (< QP)
+    float qx[RPW][2], kx[RPW][2];
 #pragma unroll
     for (int k = 0; k < RPW; k++) {
         const int ri = warp + NW * k;
@@ -346,12 +366,11 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
         qx[k][1] = in ? q[lane + 32] : 0.0f;
         kx[k][0] = in ? row[k_col + g * 64 + lane] : 0.0f;
         kx[k][1] = in ? row[k_col + g * 64 + lane + 32] : 0.0f;
-        vx[k][0] = in ? row[v_col + g * 64 + lane] : 0.0f;
-        vx[k][1] = in ? row[v_col + g * 64 + lane + 32] : 0.0f;
     }
 #pragma unroll
     for (int k = 0; k < RPW; k++) {
         const int ri = warp + NW * k;
+        if (ri >= QP) break;  // (warp-uniform)
         const float x0 = qx[k][0], x1 = qx[k][1];
         const float amax = warp_max(fmaxf(fabsf(x0), fabsf(x1)));
         const bool fin = amax <= 3.0e38f;  // inf / NaN query: every score NaN, as in the reference
@@ -360,21 +379,14 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
         int a1, a2, a3, b1, b2, b3;
         digits3(x0, mul, a1, a2, a3);
         digits3(x1, mul, b1, b2, b3);
-        // byte d of row ri -> fragment (m-tile, plane, k-step, lane g*4 + t), register
-        // 2*((w>>2)&1) + (row >= 8 within the tile), byte w & 3, with t = d/16, w = d%16
-        {
-            int8_t* qb8 = reinterpret_cast<int8_t*>(&sm.qf[0][0][0][0]);
-            const int mt = ri >> 4, g8 = ri & 7, h8 = (ri >> 3) & 1;
-#pragma unroll
-            for (int half = 0; half < 2; half++) {
-                const int d = lane + 32 * half, t = d >> 4, w = d & 15;
-                const int reg = ((w >> 2) & 1) * 2 + h8;
-                const size_t base = (((size_t)mt * 3 * 2 + (w >> 3)) * 32 + g8 * 4 + t) * 16 + reg * 4 + (w & 3);
-                const int dd[3] = {half ? b1 : a1, half ? b2 : a2, half ? b3 : a3};
-#pragma unroll
-                for (int p = 0; p < 3; p++) qb8[base + (size_t)p * 2 * 32 * 16] = (int8_t)dd[p];
-            }
-        }
+        // planes in natural dim order: the score MMA's B fragment of thread
+        // (g, t) is bytes [16t, 16t + 16) of row g of an 8-row tile
+        sm.qd[0][ri][lane] = (int8_t)a1;
+        sm.qd[1][ri][lane] = (int8_t)a2;
+        sm.qd[2][ri][lane] = (int8_t)a3;
+        sm.qd[0][ri][lane + 32] = (int8_t)b1;
+        sm.qd[1][ri][lane + 32] = (int8_t)b2;
+        sm.qd[2][ri][lane + 32] = (int8_t)b3;
         // self term with the float k and v (src/engine.cpp:760-778), in raw
         // units: (q . k) / sqrt(64) / (s / sqrt(64))
         const float sc = warp_sum(x0 * kx[k][0] + x1 * kx[k][1]) * mul;
@@ -382,15 +394,14 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
             sm.fr[ri] = f;
             sm.s_self[ri] = sc;
         }
-        sm.v_self[ri][lane] = vx[k][0];
-        sm.v_self[ri][lane + 32] = vx[k][1];
     }
 
     if (own_ex) {
 #pragma unroll
-        for (int x = 0; x < NEX; x++) {
-            const int e = (tid + 128 * x) >> 2, q4 = tid & 3;
-            if (e >= 32 * nex) break;
+        for (int x = 0; x < EXT; x++) {
+            const int task = tid + NT_THREADS * x;
+            const int e = task >> 2, q4 = task & 3;
+            if (task >= 128 * NEX || e >= 32 * nex) break;
             BlockBuf& xb = sm.ex[e >> 5];
             const int el = e & 31;
             *reinterpret_cast<uint4*>(&xb.k[el][16 * q4]) = ex_k[x];
@@ -408,26 +419,27 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
     }
     __syncthreads();
 
-    // ---- per-thread rows: (m-tile mt, half h) -> query row mt*16 + gid + 8h ----
-    float fr[MT][2], mref[MT][2], lsum[MT][2];
-    int rr[MT][2];
+    // ---- per-thread rows: thread (g, t) holds query rows 8 nt + 2t + c of every
+    // tile nt (c = 0, 1) and entries 8 j + g (j = 0..3) of each block ----
+    float fr[NT][2], mref[NT][2], lsum[NT][2];
+    int rr[NT][2];
 #pragma unroll
-    for (int mt = 0; mt < MT; mt++)
+    for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const int ri = mt * 16 + gid + 8 * h;
-            fr[mt][h] = sm.fr[ri];
-            rr[mt][h] = ri < rows ? r0 + ri % nr : -1;  // padding row: every entry has lo >= 0
-            mref[mt][h] = -INFINITY;
-            lsum[mt][h] = 0.0f;
+        for (int c = 0; c < 2; c++) {
+            const int ri = nt * 8 + 2 * tig + c;
+            fr[nt][c] = sm.fr[ri];
+            rr[nt][c] = ri < rows ? r0 + ri % nr : -1;  // padding row: every entry has lo >= 0
+            mref[nt][c] = -INFINITY;
+            lsum[nt][c] = 0.0f;  // this thread's entries only (summed over g at the end)
         }
-    float acc[MT][8][4];
+    float acc[4][NT][4];  // O^T: dims 16 dt + gid (+8 for c >= 2), rows 8 nt + 2 tig + (c & 1)
 #pragma unroll
-    for (int mt = 0; mt < MT; mt++)
+    for (int dt = 0; dt < 4; dt++)
 #pragma unroll
-        for (int nt = 0; nt < 8; nt++)
+        for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-            for (int c = 0; c < 4; c++) acc[mt][nt][c] = 0.0f;
+            for (int c = 0; c < 4; c++) acc[dt][nt][c] = 0.0f;
     int eref = 0;
     bool have_ref = false;
 
@@ -474,11 +486,11 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
             } else if (ev > eref + 4) {
                 const float c = pow2i(max(eref - ev, -126));
 #pragma unroll
-                for (int mt = 0; mt < MT; mt++)
+                for (int dt = 0; dt < 4; dt++)
 #pragma unroll
-                    for (int nt = 0; nt < 8; nt++)
+                    for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-                        for (int c4 = 0; c4 < 4; c4++) acc[mt][nt][c4] *= c;
+                        for (int c4 = 0; c4 < 4; c4++) acc[dt][nt][c4] *= c;
                 eref = ev;
             }
         }
@@ -488,138 +500,134 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
         // every row sees (no masks) and for the others.
         auto body = [&](auto full_tag) {
             constexpr bool FULL = decltype(full_tag)::value;
-            // ---- this thread's entries e = 8j + 2*tig + cc: scales (and masks) ----
-            float ksv[8], vsn[8];
-            int lo8[8], hi8[8];
+            // ---- this thread's entries e = 8 j + gid: scales (and masks) ----
+            float ksv[4], vsn[4];
+            int lo4[4], hi4[4];
 #pragma unroll
             for (int j = 0; j < 4; j++) {
-                const float2 k2 = *reinterpret_cast<const float2*>(&bb.ks[8 * j + 2 * tig]);
-                const float2 v2 = *reinterpret_cast<const float2*>(&bb.vs[8 * j + 2 * tig]);
-                ksv[2 * j] = k2.x;
-                ksv[2 * j + 1] = k2.y;
-                vsn[2 * j] = v2.x * vmul;
-                vsn[2 * j + 1] = v2.y * vmul;
-            }
-            if (!FULL) {
-#pragma unroll
-                for (int k = 0; k < 8; k++) {
-                    const int e = 8 * (k >> 1) + 2 * tig + (k & 1);
-                    lo8[k] = __shfl_sync(0xffffffffu, lo, e);
-                    hi8[k] = __shfl_sync(0xffffffffu, hi, e);
-                    if (!(hi8[k] >= 0 && lo8[k] < BIG)) vsn[k] = 0.0f;  // a masked entry must not bring a NaN scale in
+                ksv[j] = bb.ks[8 * j + gid];
+                vsn[j] = bb.vs[8 * j + gid] * vmul;
+                if (!FULL) {
+                    lo4[j] = __shfl_sync(0xffffffffu, lo, 8 * j + gid);
+                    hi4[j] = __shfl_sync(0xffffffffu, hi, 8 * j + gid);
+                    if (!(hi4[j] >= 0 && lo4[j] < BIG)) vsn[j] = 0.0f;  // a masked entry must not bring a NaN scale in
                 }
             }
 
-            // ---- scores: S = Q . K^T (three digit planes, exact int32), s_raw = S * k_scale ----
-            float s[MT][4][4];
+            // ---- scores S^T = K . Q^T (three digit planes, exact int32), s_raw = S * k_scale ----
+            // Per 16-entry m-tile: its A fragments (both k-steps) are K rows gid,
+            // gid + 8, bytes [16 tig, 16 tig + 16); the B fragments of row
+            // tile nt and plane p are bytes [16 tig, 16 tig + 16) of query row
+            // 8 nt + gid.
+            float s[2][NT][4];  // [m-tile][row tile][c]: entry 16 mt + gid + 8 (c >> 1), row 8 nt + 2 tig + (c & 1)
 #pragma unroll
-            for (int mt = 0; mt < MT; mt++) {
-                uint4 qa[3], qb[3];  // k-step 0 / 1 A fragments of each plane
+            for (int mt = 0; mt < 2; mt++) {
+                const uint4 ka = *reinterpret_cast<const uint4*>(&bb.k[16 * mt + gid][16 * tig]);
+                const uint4 kb = *reinterpret_cast<const uint4*>(&bb.k[16 * mt + gid + 8][16 * tig]);
 #pragma unroll
-                for (int p = 0; p < 3; p++) {
-                    qa[p] = sm.qf[mt][p][0][lane];
-                    qb[p] = sm.qf[mt][p][1][lane];
-                }
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    const uint4 kf = *reinterpret_cast<const uint4*>(&bb.k[8 * j + gid][16 * tig]);
+                for (int nt = 0; nt < NT; nt++) {
                     int32_t ac[3][4];
 #pragma unroll
                     for (int p = 0; p < 3; p++) {
+                        const uint4 qb = *reinterpret_cast<const uint4*>(&sm.qd[p][8 * nt + gid][16 * tig]);
                         ac[p][0] = ac[p][1] = ac[p][2] = ac[p][3] = 0;
-                        mma_s8(ac[p], qa[p].x, qa[p].y, qa[p].z, qa[p].w, kf.x, kf.y);
-                        mma_s8(ac[p], qb[p].x, qb[p].y, qb[p].z, qb[p].w, kf.z, kf.w);
+                        mma_s8(ac[p], ka.x, kb.x, ka.y, kb.y, qb.x, qb.y);
+                        mma_s8(ac[p], ka.z, kb.z, ka.w, kb.w, qb.z, qb.w);
                     }
 #pragma unroll
                     for (int c = 0; c < 4; c++) {
-                        const int k = 2 * j + (c & 1);
-                        float v = comb(ac[0][c], ac[1][c], ac[2][c]) * ksv[k];
+                        const int j = 2 * mt + (c >> 1);
+                        float v = comb(ac[0][c], ac[1][c], ac[2][c]) * ksv[j];
                         if (!FULL) {
-                            const int r = rr[mt][c >> 1];
-                            if (!(r >= lo8[k] && r <= hi8[k])) v = -INFINITY;
+                            const int r = rr[nt][c & 1];
+                            if (!(r >= lo4[j] && r <= hi4[j])) v = -INFINITY;
                         }
-                        s[mt][j][c] = v;
+                        s[mt][nt][c] = v;
                     }
                 }
             }
 
-            // ---- online softmax with a lazily raised reference maximum ----
-            float bmax[MT][2];
+            // ---- online softmax with a lazily raised reference maximum: this
+            // thread's entries decide whether any row's maximum must move ----
+            float bmax[NT][2];
             bool need = false;
 #pragma unroll
-            for (int mt = 0; mt < MT; mt++)
+            for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-                for (int h = 0; h < 2; h++) {
-                    float bm = -INFINITY;
-#pragma unroll
-                    for (int j = 0; j < 4; j++) bm = fmaxf(bm, fmaxf(s[mt][j][2 * h], s[mt][j][2 * h + 1]));
-                    bm = quad_max(bm);
-                    bmax[mt][h] = bm;
-                    const float m = mref[mt][h];
-                    need |= (bm > -INFINITY) && (m == -INFINITY || (bm - m) * fr[mt][h] > kMaxLead);
+                for (int c = 0; c < 2; c++) {
+                    const float bm = fmaxf(fmaxf(s[0][nt][c], s[0][nt][c + 2]), fmaxf(s[1][nt][c], s[1][nt][c + 2]));
+                    bmax[nt][c] = bm;
+                    const float m = mref[nt][c];
+                    need |= (bm > -INFINITY) && (m == -INFINITY || (bm - m) * fr[nt][c] > kMaxLead);
                 }
             if (__any_sync(0xffffffffu, need)) {
 #pragma unroll
-                for (int mt = 0; mt < MT; mt++)
+                for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-                    for (int h = 0; h < 2; h++) {
-                        const float m = mref[mt][h];
-                        const float mn = fmaxf(m, bmax[mt][h]);
+                    for (int c = 0; c < 2; c++) {
+                        float bm = bmax[nt][c];  // the block's maximum of the row: over gid
+                        bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 4));
+                        bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 8));
+                        bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 16));
+                        const float m = mref[nt][c];
+                        const float mn = fmaxf(m, bm);
                         if (mn > m) {
-                            const float corr = (m == -INFINITY) ? 0.0f : ex2((m - mn) * fr[mt][h]);
-                            lsum[mt][h] *= corr;
+                            const float corr = (m == -INFINITY) ? 0.0f : ex2((m - mn) * fr[nt][c]);
+                            lsum[nt][c] *= corr;
 #pragma unroll
-                            for (int nt = 0; nt < 8; nt++) {
-                                acc[mt][nt][2 * h] *= corr;
-                                acc[mt][nt][2 * h + 1] *= corr;
+                            for (int dt = 0; dt < 4; dt++) {
+                                acc[dt][nt][c] *= corr;
+                                acc[dt][nt][c + 2] *= corr;
                             }
-                            mref[mt][h] = mn;
+                            mref[nt][c] = mn;
                         }
                     }
             }
-            // p = 2^((s_raw - m) f), w = p * v_scale / 2^E -> two fp16 planes (A fragments)
-            uint32_t wa[MT][2][2][4];  // [m-tile][k-step][plane][reg]
+            // p = 2^((s_raw - m) f), w = p * v_scale / 2^E -> two fp16 planes.
+            // The pair (rows 2 tig, 2 tig + 1) of entry e is row e of an 8 x 8
+            // fp16 tile (entries x rows); movmatrix.trans turns it into the
+            // P.V MMA's B fragment (entries 2 tig, 2 tig + 1 of row gid).
+            uint32_t wb[2][NT][2][2];  // [k-step = m-tile][row tile][entry half][plane: 0 hi, 1 lo]
 #pragma unroll
-            for (int mt = 0; mt < MT; mt++) {
+            for (int mt = 0; mt < 2; mt++)
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    float w[4];
+                for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-                    for (int c = 0; c < 4; c++) {
-                        const int h = c >> 1;
-                        const float sv = s[mt][j][c];
-                        // every entry of a FULL block is visible and finite
-                        const float p = (!FULL && sv == -INFINITY) ? 0.0f : ex2((sv - mref[mt][h]) * fr[mt][h]);
-                        lsum[mt][h] += p;
-                        w[c] = p * vsn[2 * j + (c & 1)];
+                    for (int h = 0; h < 2; h++) {
+                        float w[2];
+#pragma unroll
+                        for (int c = 0; c < 2; c++) {
+                            const float sv = s[mt][nt][2 * h + c];
+                            // every entry of a FULL block is visible and finite
+                            const float p = (!FULL && sv == -INFINITY) ? 0.0f : ex2((sv - mref[nt][c]) * fr[nt][c]);
+                            lsum[nt][c] += p;
+                            w[c] = p * vsn[2 * mt + h];
+                        }
+                        const float h0 = trunc11(w[0]), h1 = trunc11(w[1]);
+                        wb[mt][nt][h][0] = movm_trans(pack_h2(h0, h1));
+                        wb[mt][nt][h][1] = movm_trans(pack_h2(w[0] - h0, w[1] - h1));
                     }
-                    const float h0 = trunc11(w[0]), h1 = trunc11(w[1]), h2 = trunc11(w[2]), h3 = trunc11(w[3]);
-                    const int ks = j >> 1, r0 = (j & 1) * 2;  // tiles 2s / 2s+1 -> a0,a1 / a2,a3
-                    wa[mt][ks][0][r0] = pack_h2(h0, h1);
-                    wa[mt][ks][0][r0 + 1] = pack_h2(h2, h3);
-                    wa[mt][ks][1][r0] = pack_h2(w[0] - h0, w[1] - h1);
-                    wa[mt][ks][1][r0 + 1] = pack_h2(w[2] - h2, w[3] - h3);
-                }
-            }
 
-            // ---- O += W . V ----
+            // ---- O^T += V^T . W^T: A = V^T (dims x entries), exact in fp16 ----
 #pragma unroll
-            for (int nt = 0; nt < 8; nt++) {
-                const uint2 vf = *reinterpret_cast<const uint2*>(&bb.v[(nt * 8 + gid) * 32 + 8 * tig]);
-                uint32_t vb[2][2];
-                i8x4_to_h2(vf.x, vb[0][0], vb[0][1]);
-                i8x4_to_h2(vf.y, vb[1][0], vb[1][1]);
+            for (int dt = 0; dt < 4; dt++) {
+                const uint2 va = *reinterpret_cast<const uint2*>(&bb.v[(16 * dt + gid) * 32 + 8 * tig]);
+                const uint2 vb = *reinterpret_cast<const uint2*>(&bb.v[(16 * dt + gid + 8) * 32 + 8 * tig]);
+                uint32_t a[2][4];  // [k-step][reg]: entries 16 ks + {2t, 2t+1} (a0 a1), + 8 (a2 a3)
+                i8x4_to_h2(va.x, a[0][0], a[0][2]);
+                i8x4_to_h2(vb.x, a[0][1], a[0][3]);
+                i8x4_to_h2(va.y, a[1][0], a[1][2]);
+                i8x4_to_h2(vb.y, a[1][1], a[1][3]);
 #pragma unroll
-                for (int mt = 0; mt < MT; mt++) {
+                for (int nt = 0; nt < NT; nt++) {
                     float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-                    for (int p = 1; p >= 0; p--)  // the remainder plane first
+                    for (int pl = 1; pl >= 0; pl--)  // the remainder plane first
 #pragma unroll
                         for (int ks = 0; ks < 2; ks++)
-                            mma_f16(o, wa[mt][ks][p][0], wa[mt][ks][p][1], wa[mt][ks][p][2], wa[mt][ks][p][3], vb[ks][0],
-                                    vb[ks][1]);
+                            mma_f16(o, a[ks][0], a[ks][1], a[ks][2], a[ks][3], wb[ks][nt][0][pl], wb[ks][nt][1][pl]);
 #pragma unroll
-                    for (int c = 0; c < 4; c++) acc[mt][nt][c] += o[c];
+                    for (int c = 0; c < 4; c++) acc[dt][nt][c] += o[c];
                 }
             }
         };
@@ -635,19 +643,22 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
     {
         const float vs_scale = pow2i(max(-126, min(126, eref)));
 #pragma unroll
-        for (int mt = 0; mt < MT; mt++)
+        for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-            for (int h = 0; h < 2; h++) {
-                const int r = mt * 16 + gid + 8 * h;
-                const float l = quad_sum(lsum[mt][h]);
-                if (tig == 0) {
-                    sm.u.merge.m[warp][r] = mref[mt][h];
+            for (int c = 0; c < 2; c++) {
+                const int r = nt * 8 + 2 * tig + c;
+                float l = lsum[nt][c];  // over the block entries of every gid
+                l += __shfl_xor_sync(0xffffffffu, l, 4);
+                l += __shfl_xor_sync(0xffffffffu, l, 8);
+                l += __shfl_xor_sync(0xffffffffu, l, 16);
+                if (gid == 0) {
+                    sm.u.merge.m[warp][r] = mref[nt][c];
                     sm.u.merge.l[warp][r] = l;
                 }
 #pragma unroll
-                for (int nt = 0; nt < 8; nt++) {
-                    sm.u.merge.acc[warp][r][nt * 8 + 2 * tig] = acc[mt][nt][h * 2] * vs_scale;
-                    sm.u.merge.acc[warp][r][nt * 8 + 2 * tig + 1] = acc[mt][nt][h * 2 + 1] * vs_scale;
+                for (int dt = 0; dt < 4; dt++) {
+                    sm.u.merge.acc[warp][r][16 * dt + gid] = acc[dt][nt][c] * vs_scale;
+                    sm.u.merge.acc[warp][r][16 * dt + gid + 8] = acc[dt][nt][c + 2] * vs_scale;
                 }
             }
     }
@@ -745,8 +756,9 @@ __global__ void __launch_bounds__(128, 2) attn_decode_kernel(KvCache kv, int lay
         }
         const float ps = ex2((ss - m) * fq);
         l += ps;
-        o0 += ps * sm.v_self[ri][lane];
-        o1 += ps * sm.v_self[ri][lane + 32];
+        const float* vrow = qkv + (size_t)(row0 + r) * ld + v_col + g * 64;  // the row's own float v
+        o0 += ps * vrow[lane];
+        o1 += ps * vrow[lane + 32];
         const float inv = 1.0f / (l + 1e-10f);
         const int row = row0 + r;
         out[(size_t)row * ldo + (size_t)h * 64 + lane] = o0 * inv;
@@ -766,26 +778,26 @@ int attention_decode_row_groups(const KvCache& kv, int H, int max_rows) {
 }
 
 int attention_decode_splits(int nb, int G, int max_splits) {
-    // Split only while the (sequence, kv head) items leave CTA slots (two per
+    // Split only while the (sequence, kv head) items leave CTA slots (four per
     // SM) empty: each split repeats the query setup and adds a merge.
     const int items = std::max(1, nb * G);
-    return std::max(1, std::min(max_splits, (2 * 148) / items));
+    return std::max(1, std::min(max_splits, (4 * 148) / items));
 }
 
 size_t attention_decode_work_floats(int nb, int G, int nsplit, int nrg) {
     return (size_t)nb * G * nrg * nsplit * QR * PART;
 }
 
-template <int MT, int NEX>
+template <int NT, int NEX>
 static pf_status launch_decode(const KvCache& kv, int layer, const RowBatch& rb, const float* qkv, int ldqkv, int k_col,
                                int v_col, int H, Staged st, SpecPool sp, const AttnWork& aw, float* out, int ldo,
                                cudaStream_t stream) {
-    const int smem = (int)sizeof(AttnSmem<MT, NEX>);
+    const int smem = (int)sizeof(AttnSmem<NT, NEX>);
     static std::atomic<uint64_t> attr{0};
-    PF_TRY(raise_smem_limit(attn_decode_kernel<MT, NEX>, smem, attr));
+    PF_TRY(raise_smem_limit(attn_decode_kernel<NT, NEX>, smem, attr));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(rb.nb, kv.G, aw.nsplit * attention_decode_row_groups(kv, H, rb.max_rows));
-    cfg.blockDim = dim3(128);
+    cfg.blockDim = dim3(NT_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute at[1];
@@ -793,7 +805,7 @@ static pf_status launch_decode(const KvCache& kv, int layer, const RowBatch& rb,
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    PF_CUDA(cudaLaunchKernelEx(&cfg, attn_decode_kernel<MT, NEX>, kv, layer, rb, qkv, ldqkv, k_col, v_col, H, st, sp, aw,
+    PF_CUDA(cudaLaunchKernelEx(&cfg, attn_decode_kernel<NT, NEX>, kv, layer, rb, qkv, ldqkv, k_col, v_col, H, st, sp, aw,
                                aw.nsplit, out, ldo, device_error_flag()));
     return launch_check("attention_decode");
 }
@@ -813,12 +825,25 @@ pf_status attention_decode(const KvCache& kv, int layer, const RowBatch& rb, con
     // one extra block for verify batches, up to NEXMAX for prefill chunks
     const int spec = rb.max_rows > 1 ? ceil_div(rb.max_rows - 1, kv.pb) + 1 : 1;
     const bool one_ex = kv.S + spec + rb.max_rows - 1 <= 32;
-    const bool mt1 = (H / kv.G) * std::min(rb.max_rows, attn_rows_per_cta(kv, H)) <= 16;
-    if (one_ex)
-        return mt1 ? launch_decode<1, 1>(kv, layer, rb, qkv, ldqkv, k_col, v_col, H, st, sp, aw, out, ldo, stream)
-                   : launch_decode<2, 1>(kv, layer, rb, qkv, ldqkv, k_col, v_col, H, st, sp, aw, out, ldo, stream);
-    return mt1 ? launch_decode<1, NEXMAX>(kv, layer, rb, qkv, ldqkv, k_col, v_col, H, st, sp, aw, out, ldo, stream)
-               : launch_decode<2, NEXMAX>(kv, layer, rb, qkv, ldqkv, k_col, v_col, H, st, sp, aw, out, ldo, stream);
+    // query rows of a CTA in 8-row tiles (the N of the score MMA)
+    const int nt = ceil_div((H / kv.G) * std::min(rb.max_rows, attn_rows_per_cta(kv, H)), 8);
+#define PF_ATTN_LAUNCH(NT_, NEX_) \
+    launch_decode<NT_, NEX_>(kv, layer, rb, qkv, ldqkv, k_col, v_col, H, st, sp, aw, out, ldo, stream)
+    if (one_ex) {
+        switch (nt) {
+            case 1: return PF_ATTN_LAUNCH(1, 1);
+            case 2: return PF_ATTN_LAUNCH(2, 1);
+            case 3: return PF_ATTN_LAUNCH(3, 1);
+            default: return PF_ATTN_LAUNCH(4, 1);
+        }
+    }
+    switch (nt) {
+        case 1: return PF_ATTN_LAUNCH(1, NEXMAX);
+        case 2: return PF_ATTN_LAUNCH(2, NEXMAX);
+        case 3: return PF_ATTN_LAUNCH(3, NEXMAX);
+        default: return PF_ATTN_LAUNCH(4, NEXMAX);
+    }
+#undef PF_ATTN_LAUNCH
 }
 
 }  // namespace pf

@@ -58,7 +58,7 @@ enum : uint32_t {
 uint32_t* device_error_flag();  // per-device global (allocated on first use)
 
 // cudaFuncSetAttribute acts on the current device's instance of a kernel, so the
-// raised dynamic shared-memory limit is recorded per device: `done` holds one bit
+// raised dynamic shared-memory limit (and the shared-memory carveout) is recorded per device: `done` holds one bit
 // per device id (< 64; above that the attribute is set on every call).
 template <typename Kernel>
 inline pf_status raise_smem_limit(Kernel kernel, size_t bytes, std::atomic<uint64_t>& done) {
@@ -67,6 +67,10 @@ inline pf_status raise_smem_limit(Kernel kernel, size_t bytes, std::atomic<uint6
     const uint64_t bit = dev < 64 ? (1ull << dev) : 0ull;
     if (bit && (done.load(std::memory_order_acquire) & bit)) return PF_OK;
     PF_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+    // all of the unified L1 / shared array as shared memory, so that as many
+    // CTAs as the registers allow fit on an SM
+    PF_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 (int)cudaSharedmemCarveoutMaxShared));
     done.fetch_or(bit, std::memory_order_acq_rel);
     return PF_OK;
 }
