@@ -29,34 +29,26 @@ __device__ __forceinline__ float warp_max(float v) {
     for (int o = 16; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
 }
-// Block sum in the device order; every thread gets the result.
+// Block sum in the device order; every thread gets the result.  Each warp
+// publishes its xor-butterfly total, and after one barrier every thread adds
+// the totals itself in warp order (the sequence thread 0 used to add them in,
+// so the result is the same).  Sums use sh[0..7], maxima sh[16..23]: a kernel
+// may take one of each without a barrier in between.
 __device__ __forceinline__ float block_sum(float v, float* sh) {
     v = warp_sum_xor(v);
-    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
     __syncthreads();
-    if ((threadIdx.x & 31) == 0) sh[w] = v;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float t = sh[0];
-        for (int i = 1; i < (int)(blockDim.x >> 5); i++) t = __fadd_rn(t, sh[i]);
-        sh[32] = t;
-    }
-    __syncthreads();
-    return sh[32];
+    float t = sh[0];
+    for (int i = 1; i < (int)(blockDim.x >> 5); i++) t = __fadd_rn(t, sh[i]);
+    return t;
 }
 __device__ __forceinline__ float block_max(float v, float* sh) {
     v = warp_max(v);
-    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) sh[16 + (threadIdx.x >> 5)] = v;
     __syncthreads();
-    if ((threadIdx.x & 31) == 0) sh[w] = v;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float t = sh[0];
-        for (int i = 1; i < (int)(blockDim.x >> 5); i++) t = fmaxf(t, sh[i]);
-        sh[32] = t;
-    }
-    __syncthreads();
-    return sh[32];
+    float t = sh[16];
+    for (int i = 1; i < (int)(blockDim.x >> 5); i++) t = fmaxf(t, sh[16 + i]);
+    return t;
 }
 
 // quantize_activation_row (src/matmul_neon.cpp:16-29): mul = 127/amax,
@@ -195,6 +187,32 @@ __global__ void __launch_bounds__(RT) quant_rows_kernel(const float* __restrict_
     const int row = blockIdx.x, t = threadIdx.x;
     if (!row_active(row, M, m_dev)) return;
     const float* xr = x + (size_t)row * ldx;
+    if ((n & 3) == 0 && (ldx & 3) == 0 && (ldq & 3) == 0 && n <= RT * EPT &&
+        ((reinterpret_cast<uintptr_t>(x) & 15) | (reinterpret_cast<uintptr_t>(q) & 3)) == 0) {
+        // 16-byte loads and 4-byte stores: thread t owns columns 4 (t + RT i) .. +3
+        constexpr int E4 = EPT / 4;
+        float4 v4[E4];
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < E4; i++) {
+            const int c = 4 * (t + i * RT);
+            v4[i] = c < n ? *reinterpret_cast<const float4*>(xr + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v4[i].x), fabsf(v4[i].y)), fmaxf(fabsf(v4[i].z), fabsf(v4[i].w))));
+        }
+        amax = block_max(amax, sh);
+        float mul, scale;
+        row_quant_params(amax, mul, scale);
+        int8_t* qr = q + (size_t)row * ldq;
+#pragma unroll
+        for (int i = 0; i < E4; i++) {
+            const int c = 4 * (t + i * RT);
+            if (c < n)
+                *reinterpret_cast<char4*>(qr + c) =
+                    make_char4(q8(v4[i].x, mul), q8(v4[i].y, mul), q8(v4[i].z, mul), q8(v4[i].w, mul));
+        }
+        if (t == 0) qs[row] = scale;
+        return;
+    }
     float v[EPT];
     float amax = 0.0f;
 #pragma unroll
