@@ -299,6 +299,8 @@ def main():
         torch.cuda.nvtx.range_push("prefill")  # (a range for profilers; free otherwise)
         eng.prefill(host_prompts, seeds)
         torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()  # (the first step needs the prefill's result anyway)
+        t_pre = time.perf_counter() - t0
         got = seqs  # the first token comes out of prefill
         for _ in range(args.steps):
             n, em = eng.step()
@@ -306,7 +308,7 @@ def main():
         torch.cuda.synchronize()
         el = time.perf_counter() - t0
         el, got = replicas.step_totals(el, got)
-        e2e = {"value": got / el, "unit": UNIT,
+        e2e = {"value": got / el, "unit": UNIT, "prefill_ms": round(t_pre * 1e3, 2),
                "h2d_bytes_per_step": int(seqs * plen * 4 / max(1, args.steps)),
                "d2h_bytes_per_step": int(seqs * (R + 1) * 4),
                "includes": f"prefill of {seqs}x{plen} prompt tokens from pinned host memory + {args.steps} "

@@ -74,6 +74,10 @@ namespace pf {
 namespace {
 
 constexpr int QR = 32;   // query rows per CTA at most
+// Query rows a CTA takes: 24 (three 8-row tiles) while the q heads sharing a
+// kv head fit, so that wide batches (prefill chunks) also run the 168-register
+// kernel at four CTAs per SM; 32 otherwise.
+__host__ __device__ inline int cta_query_rows(int qpk) { return qpk <= 24 ? 24 : QR; }
 constexpr int ACC_STRIDE = 68;  // floats per row of the warps' merge sums
 constexpr int NW = 3;    // warps per CTA (3: four CTAs fit an SM, one wave for 512 units)
 constexpr int NT_THREADS = 32 * NW;
@@ -228,7 +232,7 @@ __global__ void __launch_bounds__(NT_THREADS, NT <= 3 ? 4 : 2) attn_decode_kerne
     const int split = (int)blockIdx.z % nsplit, rg = (int)blockIdx.z / nsplit;
     const int n = rb.n[b];
     const int qpk = H / kv.G;
-    const int rpc = QR / qpk;      // sequence rows per CTA
+    const int rpc = cta_query_rows(qpk) / qpk;  // sequence rows per CTA
     const int r0 = rg * rpc;       // this CTA's sequence rows [r0, r0 + nr)
     if (r0 >= n) {
         // (every CTA waits for the previous kernel, so that this grid's
@@ -772,7 +776,8 @@ bool attention_decode_supported(const KvCache& kv, int H, int max_rows) {
 }
 
 // Sequence rows per CTA and row groups per (sequence, kv head).
-static int attn_rows_per_cta(const KvCache& kv, int H) { return QR / (H / kv.G); }
+static int attn_rows_per_cta(const KvCache& kv, int H) { return cta_query_rows(H / kv.G) / (H / kv.G); }
+int attention_decode_rows_per_cta(const KvCache& kv, int H) { return attn_rows_per_cta(kv, H); }
 int attention_decode_row_groups(const KvCache& kv, int H, int max_rows) {
     return ceil_div(std::max(1, max_rows), attn_rows_per_cta(kv, H));
 }

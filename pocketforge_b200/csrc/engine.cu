@@ -944,6 +944,10 @@ pf_status pf_engine_prefill(pf_engine* e, int32_t n, const int32_t* tokens, cons
     // (at most as many rows per sequence as the tensor-core attention takes)
     int C = std::max(1, std::min(e->kv.Wr, e->Mcap / n));
     while (C > 1 && !attention_decode_supported(e->kv, e->H, C)) C--;
+    {
+        const int rpc = attention_decode_rows_per_cta(e->kv, e->H);  // whole row groups per chunk
+        if (C > rpc) C -= C % rpc;
+    }
     std::vector<int> row_tok, row_pos, row0(n), cnt(n), len0(n), last_idx(n, -1);
     std::vector<float> dummy;
     for (int c0 = 0; c0 < maxlen; c0 += C) {

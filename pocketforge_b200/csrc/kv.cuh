@@ -97,6 +97,9 @@ struct AttnWork {
     size_t cnt_elems = 0;
 };
 bool attention_decode_supported(const KvCache& kv, int H, int max_rows);
+// Sequence rows one attention CTA takes (a batch's rows per sequence split
+// into row groups of this many).
+int attention_decode_rows_per_cta(const KvCache& kv, int H);
 int attention_decode_splits(int nb, int G, int max_splits);
 int attention_decode_row_groups(const KvCache& kv, int H, int max_rows);
 size_t attention_decode_work_floats(int nb, int G, int nsplit, int nrg);
