@@ -124,13 +124,24 @@ def kv_entry_bytes(model):
     return model.n_layers * model.n_kv_heads * (2 * model.head_dim + 8)
 
 
+def attended_entries(model, ctx):
+    """KV entries a query at context length ctx attends: the sinks, the
+    window, and one pooled entry per pool_block positions beyond them (the
+    3-tier cache, src/kv_cache.cpp:129-198)."""
+    S, W, pb = model.sink_size, model.window_size, model.pool_block
+    sink = min(ctx, S)
+    win = min(max(ctx - S, 0), W)
+    pool = max(ctx - S - W, 0) // pb
+    return sink + win + pool
+
+
 def algorithmic_bytes_per_step(model, n_seqs, ctx_avg, committed_per_step, K):
     """Bytes a verify step must move (weights, LM head, MTP heads, attended
     int8 KV, committed KV writes); activations stay on chip / in L2."""
     W = model.weight_bytes()
     E = model.n_vocab * model.n_embd // 2 if model.emb_qtype == 1 else model.n_vocab * model.n_embd
     H = K * 3 * model.n_embd * model.n_embd // 2 + K * 3 * model.n_embd * 4
-    kv_read = n_seqs * ctx_avg * kv_entry_bytes(model)
+    kv_read = n_seqs * attended_entries(model, ctx_avg) * kv_entry_bytes(model)
     kv_write = committed_per_step * kv_entry_bytes(model)
     return W + E + H + kv_read + kv_write
 
@@ -381,10 +392,11 @@ def main():
     # all sequences; algorithmic bytes = attended entries x 8 kv heads x
     # (64 K + 64 V + 2 fp32 scales) for one layer.
     ctx_mid = float(((pos0 + pos1) / 2 + 2 * R).mean())  # the timing steps ran after the timed region
-    attn_bytes = seqs * ctx_mid * model.n_kv_heads * (2 * model.head_dim + 8)
+    attn_bytes = seqs * attended_entries(model, ctx_mid) * model.n_kv_heads * (2 * model.head_dim + 8)
     attn_us = attn_ms * 1e3 / max(1, attn_n)
     attn_gbs = attn_bytes / (attn_us * 1e-6) / 1e9
-    proj_bytes = bytes_step - seqs * ctx_avg * kv_entry_bytes(model) - committed * kv_entry_bytes(model)
+    proj_bytes = bytes_step - seqs * attended_entries(model, ctx_avg) * kv_entry_bytes(model) - \
+        committed * kv_entry_bytes(model)
     proj_ops = projection_ops_per_step(model, seqs * R, seqs, K)
     traffic = profiled_traffic()
     clocks = clk.summary()
@@ -408,13 +420,13 @@ def main():
             "verify_step_us": step_ms * 1e3,
             "roofline": {"bound": "hbm", "achieved": attn_gbs, "peak": peak, "unit": "GB/s",
                          "frac": attn_gbs / peak, "peak_kind": peak_kind,
-                         "traffic": traffic.get("attn_decode_per_seq_entry", 0.0) * seqs * ctx_mid or None,
+                         "traffic": traffic.get("attn_decode_per_seq_entry", 0.0) * seqs * attended_entries(model, ctx_mid) or None,
                          "kernel": "attn_decode_kernel: one layer's attention, all sequences x 8 kv heads",
                          "algorithmic_bytes_per_launch": attn_bytes, "launch_us": attn_us,
                          "launches_timed": attn_n,
                          "step": {"achieved": achieved, "frac": achieved / peak,
                                   "algorithmic_bytes_per_step": bytes_step,
-                                  "traffic": traffic.get("step_per_seq_entry", 0.0) * seqs * ctx_avg
+                                  "traffic": traffic.get("step_per_seq_entry", 0.0) * seqs * attended_entries(model, ctx_avg)
                                   + traffic.get("step_fixed", 0.0) or None,
                                   "unit_of_work": "one verify step (CUDA graph launch)"},
                          "projections": {"ms_per_step": proj_ms, "launches": proj_n,
