@@ -584,6 +584,17 @@ pf_status put_draft(const int* tok, int n, int K, int h, int* drafts, cudaStream
     put_draft_kernel<<<ceil_div(n, 128), 128, 0, st>>>(tok, n, K, h, drafts);
     return launch_check("put_draft");
 }
+// Every head at once: drafts[b][h] = tok[h * stride + b].
+__global__ void put_drafts_kernel(const int* __restrict__ tok, int n, int K, int stride, int* __restrict__ drafts) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n * K) return;
+    const int b = i / K, h = i % K;
+    drafts[i] = tok[(size_t)h * stride + b];
+}
+pf_status put_drafts(const int* tok, int n, int K, int stride, int* drafts, cudaStream_t st) {
+    put_drafts_kernel<<<ceil_div(n * K, 128), 128, 0, st>>>(tok, n, K, stride, drafts);
+    return launch_check("put_drafts");
+}
 
 // ---------------------------------------------------------------------------
 // Predictive FFN skip (LayerSkipController::should_skip_ffn,

@@ -112,7 +112,9 @@ struct pf_engine {
     float* mtp_in = nullptr;   // [max_seqs][d] MTP input (hidden of the row that produced `pending`)
     float* mtp_cur = nullptr;
     float* mtp_logits = nullptr;
-    int* mtp_tok = nullptr;
+    int* mtp_tok = nullptr;            // [K][max_seqs]
+    int8_t* mdig = nullptr;            // every head's output digit planes, [3][K * max_seqs][d]
+    float* mdscale = nullptr;          // [K * max_seqs]
     int* next = nullptr;
     int* iota = nullptr;
     int* last_row = nullptr;
@@ -359,6 +361,7 @@ struct pf_engine {
     // result for the next one (the head's residual output also feeds the
     // unembedding and the next head).
     pf_status mtp_chain(int n) {
+        if (K == 0 || n == 0) return PF_OK;
         const int64_t plane = (int64_t)n * d;
         PF_TRY(split_digits(mtp_cur, d, d, n, nullptr, digits, plane, d, dscale, st));
         for (int h = 0; h < K; h++) {
@@ -368,25 +371,31 @@ struct pf_engine {
                               dscale, st));
             PF_TRY(mtp_gemm(mtp_down[h], d, n, &parts));
             PF_TRY(mtp_finish(false, rws, parts, (int64_t)3 * n * d, dscale, mtp_down_s[h], d, n, mtp_cur, digits,
-                              dscale, st));
-            float* lg = mtp_logits + (size_t)h * max_seqs * V;
-            {
-                GemmParams p;
-                p.A = digits; p.plane_stride = plane; p.lda = d; p.a_scale = dscale; p.M = n; p.N = V; p.K = d;
-                p.W = emb_packed; p.wf = fmt_emb; p.w_scale_all = emb_gscale;
-                p.epi = EPI_LOGITS3; p.out = lg; p.ldo = V;
-                p.splits = 1;
-                p.pdl = true;
-                PF_TRY(tbegin(1));
-                PF_TRY(gemm_tc_launch(p, 3, n, st));
-                PF_TRY(tend());
-            }
+                              dscale, st, mdig + (size_t)h * max_seqs * d, (int64_t)K * max_seqs * d,
+                              mdscale + (size_t)h * max_seqs));
+        }
+        // The heads' unembeddings depend only on their own hidden states, so
+        // they run as one launch over every head's rows (K * max_seqs rows,
+        // rows h * max_seqs + b), not as K launches of n rows each.
+        {
+            const int MK = K * max_seqs;
+            GemmParams p;
+            p.A = mdig; p.plane_stride = (int64_t)MK * d; p.lda = d; p.a_scale = mdscale; p.M = MK; p.N = V; p.K = d;
+            p.W = emb_packed; p.wf = fmt_emb; p.w_scale_all = emb_gscale;
+            p.epi = EPI_LOGITS3; p.out = mtp_logits; p.ldo = V;
+            p.splits = 1;
+            p.pdl = true;
+            PF_TRY(tbegin(1));
+            PF_TRY(gemm_tc_launch(p, 3, MK, st));
+            PF_TRY(tend());
             if (greedy()) {
-                PF_TRY(argmax_rows(lg, V, V, n, nullptr, mtp_tok, st));
+                PF_TRY(argmax_rows(mtp_logits, V, V, MK, nullptr, mtp_tok, st));
             } else {
-                PF_TRY(sample_rows(lg, V, V, iota, n, samp, cur_u + 1 + h, R, mtp_tok, st));
+                for (int h = 0; h < K; h++)
+                    PF_TRY(sample_rows(mtp_logits + (size_t)h * max_seqs * V, V, V, iota, n, samp, cur_u + 1 + h, R,
+                                       mtp_tok + (size_t)h * max_seqs, st));
             }
-            PF_TRY(put_draft(mtp_tok, n, K, h, sb.drafts, st));
+            PF_TRY(put_drafts(mtp_tok, n, K, max_seqs, sb.drafts, st));
         }
         return PF_OK;
     }
@@ -654,7 +663,13 @@ pf_status pf_engine_create(const pf_model_config* c, int32_t max_seqs, int32_t m
     E_TRY(dalloc(&e->mtp_in, (size_t)max_seqs * d, o));
     E_TRY(dalloc(&e->mtp_cur, (size_t)max_seqs * d, o));
     E_TRY(dalloc(&e->mtp_logits, (size_t)e->K * max_seqs * V, o));
-    E_TRY(dalloc(&e->mtp_tok, max_seqs, o));
+    E_TRY(dalloc(&e->mtp_tok, (size_t)e->K * max_seqs, o));
+    E_TRY(dalloc(&e->mdig, (size_t)3 * e->K * max_seqs * d, o));
+    E_TRY(dalloc(&e->mdscale, (size_t)e->K * max_seqs, o));
+    // rows of sequences not in a batch stay finite (zero digits and scales)
+    if (cudaMemset(e->mdig, 0, (size_t)3 * e->K * max_seqs * d) != cudaSuccess ||
+        cudaMemset(e->mdscale, 0, (size_t)e->K * max_seqs * sizeof(float)) != cudaSuccess)
+        return fail(PF_ERR_CUDA);
     E_TRY(dalloc(&e->next, max_seqs, o));
     E_TRY(dalloc(&e->iota, max_seqs, o));
     E_TRY(dalloc(&e->last_row, max_seqs, o));

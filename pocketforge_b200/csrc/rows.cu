@@ -329,7 +329,8 @@ template <bool SWIGLU>
 __global__ void __launch_bounds__(RT) mtp_finish_kernel(const int32_t* __restrict__ parts, int n_parts,
                                                         int64_t part_stride, const float* a_s,
                                                         const float* __restrict__ w_s, int d, int M,
-                                                        float* __restrict__ x, int8_t* __restrict__ q, float* qs) {
+                                                        float* __restrict__ x, int8_t* __restrict__ q, float* qs,
+                                                        int8_t* __restrict__ q2, int64_t plane2, float* qs2) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // lets the next GEMM start its prologue
     __shared__ float sh[33];
     const int row = blockIdx.x, t = threadIdx.x;
@@ -421,21 +422,34 @@ __global__ void __launch_bounds__(RT) mtp_finish_kernel(const int32_t* __restric
         q[o] = (int8_t)(int)d1;
         q[o + plane] = (int8_t)(int)d2;
         q[o + 2 * plane] = (int8_t)(int)d3;
+        if (q2) {
+            q2[o] = (int8_t)(int)d1;
+            q2[o + plane2] = (int8_t)(int)d2;
+            q2[o + 2 * plane2] = (int8_t)(int)d3;
+        }
     }
-    if (t == 0) qs[row] = !isfinite(amax) ? __int_as_float(0x7fc00000) : (amax == 0.0f) ? 1.0f : __fdiv_rn(amax, 127.0f);
+    if (t == 0) {
+        const float sc = !isfinite(amax) ? __int_as_float(0x7fc00000) : (amax == 0.0f) ? 1.0f : __fdiv_rn(amax, 127.0f);
+        qs[row] = sc;
+        if (qs2) qs2[row] = sc;
+    }
 }
 
 pf_status mtp_finish(bool swiglu, const int32_t* parts, int n_parts, int64_t part_stride, const float* a_s,
-                     const float* w_s, int d, int M, float* x, int8_t* q, float* qs, cudaStream_t st) {
+                     const float* w_s, int d, int M, float* x, int8_t* q, float* qs, cudaStream_t st, int8_t* q2,
+                     int64_t plane2, float* qs2) {
+    PF_CHECK(!q2 || (qs2 && plane2 >= (int64_t)M * d), "mtp_finish: bad second copy");
     PF_CHECK(d <= RT * 8, "mtp_finish: row length %d above %d", d, RT * 8);
     PF_CHECK(n_parts >= 1 && n_parts <= kMtpMaxParts &&
                  part_stride >= (int64_t)3 * M * (swiglu ? 2 * d : d),
              "mtp_finish: bad slices");
     PF_CHECK(swiglu || x, "mtp_finish: the residual form needs x");
     if (swiglu)
-        mtp_finish_kernel<true><<<M, RT, 0, st>>>(parts, n_parts, part_stride, a_s, w_s, d, M, x, q, qs);
+        mtp_finish_kernel<true><<<M, RT, 0, st>>>(parts, n_parts, part_stride, a_s, w_s, d, M, x, q, qs, q2, plane2,
+                                                  qs2);
     else
-        mtp_finish_kernel<false><<<M, RT, 0, st>>>(parts, n_parts, part_stride, a_s, w_s, d, M, x, q, qs);
+        mtp_finish_kernel<false><<<M, RT, 0, st>>>(parts, n_parts, part_stride, a_s, w_s, d, M, x, q, qs, q2, plane2,
+                                                   qs2);
     return launch_check("mtp_finish");
 }
 

@@ -22,9 +22,11 @@ pf_status quant_rows_given(const float* x, int n, int M, const float* s, int8_t*
 // An MTP head projection's finish from K-split slices of its stacked digit-plane
 // rows ([parts][3 M][N]): the GEMM epilogue's arithmetic (SwiGLU over (gate, up)
 // column pairs, N = 2 d; or the residual x += value, N = d), then the three
-// digit planes of the resulting rows into q ([3][M][d]) and qs.
+// digit planes of the resulting rows into q ([3][M][d]) and qs, and, if q2 is
+// given, a second copy into q2 (planes plane2 apart) and qs2.
 pf_status mtp_finish(bool swiglu, const int32_t* parts, int n_parts, int64_t part_stride, const float* a_s,
-                     const float* w_s, int d, int M, float* x, int8_t* q, float* qs, cudaStream_t st);
+                     const float* w_s, int d, int M, float* x, int8_t* q, float* qs, cudaStream_t st,
+                     int8_t* q2 = nullptr, int64_t plane2 = 0, float* qs2 = nullptr);
 pf_status split_digits(const float* x, int n, int ldx, int M, const int* m_dev, int8_t* q, int64_t plane,
                        int ldq, float* qs, cudaStream_t st);
 pf_status embed(const int8_t* emb, float gscale, int d, int V, const int* tok, int M, const int* m_dev, float* x,

@@ -32,6 +32,8 @@ pf_status sample_rows(const float* logits, int ld, int V, const int* rows, int n
                       const float* uniforms, int ustride, int* out, cudaStream_t st);
 pf_status pick(const int* src, const int* idx, int n, int* out, cudaStream_t st);
 pf_status put_draft(const int* tok, int n, int K, int h, int* drafts, cudaStream_t st);
+// drafts[b][h] = tok[h * stride + b] for every head h < K and sequence b < n.
+pf_status put_drafts(const int* tok, int n, int K, int stride, int* drafts, cudaStream_t st);
 pf_status skip_decide(int nb, const int* bs_row0, const int* bs_n, int max_rows, const float* normed, int d,
                       const float* cache, size_t cache_stride, float thr_l, uint8_t* skip, cudaStream_t st);
 pf_status skip_commit(int nb, int L, int d, int Mst, const int* bs_row0, const int* n_commit, const uint8_t* skip_all,
