@@ -3,7 +3,9 @@
 // (tcgen05.mma.kind::i8), with the epilogues of gemm.cuh.
 //
 // One CTA computes a 128-row x BN-column output tile (BN = 64, 128 or 256;
-// optionally one split of K).  Per 128-wide K stage:
+// optionally one split of K), or TM = 2 such tiles stacked in M that share
+// every unpacked weight stage (prefill-sized SwiGLU launches).  Per 128-wide
+// K stage:
 //   warp 0: lane s*(P+1)+c issues copy c of every stage that uses load slot
 //     s — the activation tile of digit plane c (128 x 128 B, 128-byte
 //     swizzle) or, for c == P, the packed weight block (BN rows x RB bytes)
@@ -152,17 +154,17 @@ __host__ __device__ constexpr int row_bytes() {
     return WF == WF_Q4 ? 64 : (WF == WF_Q2 ? 32 : 128);
 }
 
-template <int BN, int P, int WF>
+template <int BN, int P, int WF, int TM = 1>
 struct Layout {
-    static constexpr int A_BYTES = BM * BK;             // one plane
+    static constexpr int A_BYTES = BM * BK;             // one plane of one 128-row M tile
     static constexpr int RAW_BYTES = BN * row_bytes<WF>();
     static constexpr int B_BYTES = BN * BK;
     // Load ring: STAGES slots of activation planes + packed weights (what the
     // TMA has in flight); the unpacked weights get NB buffers of their own,
     // so the ring can be deeper than the unpack -> MMA hand-off needs.
-    static constexpr int SLOT_BYTES = P * A_BYTES + ((RAW_BYTES + 1023) / 1024) * 1024;
+    static constexpr int SLOT_BYTES = TM * P * A_BYTES + ((RAW_BYTES + 1023) / 1024) * 1024;
     static constexpr int NB = 2;
-    static constexpr int STAGES_MAX = (P == 1) ? 8 : 4;
+    static constexpr int STAGES_MAX = (P * TM == 1) ? 8 : 4;
     static constexpr int BUDGET = 220 * 1024;
     static constexpr int FIT = (BUDGET - NB * B_BYTES) / SLOT_BYTES;
     static constexpr int STAGES = STAGES_MAX < FIT ? STAGES_MAX : FIT;
@@ -173,8 +175,9 @@ struct Layout {
     // Epilogue staging (reuses the rings): 8 warps x 32 rows x (BN/2 + 4) fp32.
     static constexpr int SROW = BN / 2 + 4;
     static_assert(8 * 32 * SROW * 4 <= BAR_OFF, "staging does not fit the rings");
-    static constexpr int TMEM_COLS = (P * BN <= 32) ? 32 : (P * BN <= 64) ? 64 : (P * BN <= 128) ? 128
-                                    : (P * BN <= 256) ? 256 : 512;
+    static constexpr int TMEM_COLS = (TM * P * BN <= 32) ? 32 : (TM * P * BN <= 64) ? 64
+                                    : (TM * P * BN <= 128) ? 128 : (TM * P * BN <= 256) ? 256 : 512;
+    static_assert(TM * P * BN <= 512, "accumulators exceed TMEM");
 };
 
 template <int P>
@@ -289,11 +292,11 @@ __device__ __forceinline__ void store_rows(const GemmParams& p, const float* stg
     }
 }
 
-template <int BN, int P, int WF, int EPI>
+template <int BN, int P, int WF, int EPI, int TM = 1>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmParams p,
                    int plane_rows, uint32_t* err) {
-    using Ly = Layout<BN, P, WF>;
+    using Ly = Layout<BN, P, WF, TM>;
     constexpr int STAGES = Ly::STAGES;
     constexpr int RB = row_bytes<WF>();
     constexpr int SHIFT = WF == WF_Q4 ? 4 : (WF == WF_Q2 ? 6 : 0);  // weight position inside its byte
@@ -311,8 +314,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Ly::BAR_OFF + 8 * (2 * STAGES + 2 * NB + 1));
     volatile int* abort_flag =
         reinterpret_cast<volatile int*>(smem + Ly::BAR_OFF + 8 * (2 * STAGES + 2 * NB + 1) + 8);
-    auto a_addr = [&](int s, int pl) { return sbase + (uint32_t)(s * Ly::SLOT_BYTES + pl * Ly::A_BYTES); };
-    auto raw_addr = [&](int s) { return sbase + (uint32_t)(s * Ly::SLOT_BYTES + P * Ly::A_BYTES); };
+    // slot s: activation tiles (M tile t, plane pl) at index t * P + pl, then the packed weights
+    auto a_addr = [&](int s, int pl, int t = 0) {
+        return sbase + (uint32_t)(s * Ly::SLOT_BYTES + (t * P + pl) * Ly::A_BYTES);
+    };
+    auto raw_addr = [&](int s) { return sbase + (uint32_t)(s * Ly::SLOT_BYTES + TM * P * Ly::A_BYTES); };
     auto b_addr = [&](int b) { return sbase + (uint32_t)(Ly::B_OFF + b * Ly::B_BYTES); };
 
     // The next kernel may start its prologue now; it waits for this grid's
@@ -323,7 +329,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         prefetch_map(&tmB);
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM * TM;  // TM tiles of 128 rows share each weight stage
     const int nkt = p.K / BK;
     const int per = (nkt + p.splits - 1) / p.splits;
     const int kt0 = blockIdx.z * per, kt1 = min(nkt, kt0 + per);
@@ -331,7 +337,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
-            mbar_init(full_raw(s), P + 1);  // one arrival per issuing lane
+            mbar_init(full_raw(s), TM * P + 1);  // one arrival per issuing lane
             mbar_init(empty(s), 1);
         }
         for (int b = 0; b < NB; b++) {
@@ -363,15 +369,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // each (slot, copy) pair has its own lane: lane s*(P+1)+c issues copy
         // c (activation plane c, or the packed weights for c == P) of every
         // stage that uses slot s, and arrives on full_raw[s] with its bytes.
-        constexpr int COPIES = P + 1;
+        constexpr int COPIES = TM * P + 1;  // activation tiles of every (M tile, plane), then the weights
         static_assert(STAGES * COPIES <= 32, "one lane per (slot, copy)");
         if (lane < STAGES * COPIES) {
             const int s = lane / COPIES, c = lane % COPIES;
-            const uint32_t bytes = (uint32_t)(c < P ? Ly::A_BYTES : Ly::RAW_BYTES);
+            const uint32_t bytes = (uint32_t)(c < TM * P ? Ly::A_BYTES : Ly::RAW_BYTES);
             // Activations come from the previous kernel: under programmatic
             // dependent launch, wait for it.  Weights do not, so their
             // copies may start while it finishes.
-            if (c < P) asm volatile("griddepcontrol.wait;" ::: "memory");
+            if (c < TM * P) asm volatile("griddepcontrol.wait;" ::: "memory");
             int last = -1;
             for (int i = s; i < nst && !*abort_flag; i += STAGES) {
                 if (!mbar_wait(empty(s), ((i / STAGES) & 1) ^ 1)) {
@@ -380,8 +386,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
                 const int kt = kt0 + i;
                 mbar_expect_tx(full_raw(s), bytes);
-                if (c < P)
-                    tma_load_2d(a_addr(s, c), &tmA, kt * BK, c * plane_rows + m0, full_raw(s));
+                if (c < TM * P)  // tile c / P, plane c % P (rows past M read as zeros)
+                    tma_load_2d(a_addr(s, c % P, c / P), &tmA, kt * BK, (c % P) * plane_rows + m0 + (c / P) * BM,
+                                full_raw(s));
                 else
                     tma_load_2d(raw_addr(s), &tmB, 0, kt * p.N + n0, full_raw(s));
                 last = i;
@@ -408,12 +415,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 asm volatile("tcgen05.fence::after_thread_sync;");
                 const uint64_t bd = sw128_desc(b_addr(b));
 #pragma unroll
-                for (int pl = 0; pl < P; pl++) {
-                    const uint64_t ad = sw128_desc(a_addr(s, pl));
+                for (int tt = 0; tt < TM; tt++)  // every M tile against the one unpacked weight stage
 #pragma unroll
-                    for (int kk = 0; kk < BK / 32; kk++)  // K = 32 bytes per MMA: +2 in 16-byte units
-                        umma_i8(tmem + (uint32_t)(pl * BN), ad + 2 * kk, bd + 2 * kk, idesc, (i > 0 || kk > 0) ? 1u : 0u);
-                }
+                    for (int pl = 0; pl < P; pl++) {
+                        const uint64_t ad = sw128_desc(a_addr(s, pl, tt));
+#pragma unroll
+                        for (int kk = 0; kk < BK / 32; kk++)  // K = 32 bytes per MMA: +2 in 16-byte units
+                            umma_i8(tmem + (uint32_t)((tt * P + pl) * BN), ad + 2 * kk, bd + 2 * kk, idesc,
+                                    (i > 0 || kk > 0) ? 1u : 0u);
+                    }
                 umma_commit(empty(s));
                 umma_commit(b_empty(b));
             }
@@ -493,9 +503,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // the tile's columns.
         const int sub = warp & 3;
         const int c0 = ((warp - 2) >> 2) * HALF;
-        const int m = m0 + sub * 32 + lane;
+        for (int tt = 0; tt < TM; tt++) {  // the CTA's M tiles, one after another (TM > 1: no split K)
+        const int m0t = m0 + tt * BM;
+        const int m = m0t + sub * 32 + lane;
         const bool in_m = m < p.M;
-        const uint32_t tbase = tmem + ((uint32_t)(sub * 32) << 16);
+        const uint32_t tbase = tmem + ((uint32_t)(sub * 32) << 16) + (uint32_t)(tt * P * BN);
         bool write_tile = ok;
         if (ok && p.splits > 1 && p.slice_stride == 0) {
             // Split-K: every split adds its partial sums into the workspace,
@@ -595,9 +607,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             // Slices mode: split z writes its own int32 tile (reduced later).
             int32_t* oi = p.out_i32 ? p.out_i32 + (size_t)blockIdx.z * p.slice_stride : nullptr;
             if constexpr (SWI)
-                store_rows<HALF / 2, Ly::SROW, EPI>(p, stg, m0 + sub * 32, (n0 + c0) >> 1, lane, oi);
+                store_rows<HALF / 2, Ly::SROW, EPI>(p, stg, m0t + sub * 32, (n0 + c0) >> 1, lane, oi);
             else
-                store_rows<HALF, Ly::SROW, EPI>(p, stg, m0 + sub * 32, n0 + c0, lane, oi);
+                store_rows<HALF, Ly::SROW, EPI>(p, stg, m0t + sub * 32, n0 + c0, lane, oi);
+        }
+        __syncwarp();  // this warp's staging rows are read before the next tile's pass 1 writes them
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;");
@@ -645,9 +659,9 @@ pf_status make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t 
     return PF_OK;
 }
 
-template <int BN, int P, int WF, int EPI>
+template <int BN, int P, int WF, int EPI, int TM = 1>
 pf_status launch_tc(const GemmParams& p, int plane_rows, cudaStream_t st) {
-    using Ly = Layout<BN, P, WF>;
+    using Ly = Layout<BN, P, WF, TM>;
     static_assert(Ly::STAGES >= 2, "shared memory budget too small");
     CUtensorMap ta, tb;
     const uint64_t a_rows = (P == 1) ? (uint64_t)p.M : (uint64_t)P * plane_rows;
@@ -655,8 +669,8 @@ pf_status launch_tc(const GemmParams& p, int plane_rows, cudaStream_t st) {
     PF_TRY(make_map(&tb, p.W, (uint64_t)row_bytes<WF>(), (uint64_t)(p.K / BK) * p.N, (uint64_t)row_bytes<WF>(),
                     row_bytes<WF>(), BN, CU_TENSOR_MAP_SWIZZLE_NONE));
     static std::atomic<uint64_t> attr{0};
-    PF_TRY(raise_smem_limit(gemm_tc_kernel<BN, P, WF, EPI>, Ly::SMEM, attr));
-    dim3 grid(p.N / BN, ceil_div(p.M, BM), p.splits);
+    PF_TRY(raise_smem_limit(gemm_tc_kernel<BN, P, WF, EPI, TM>, Ly::SMEM, attr));
+    dim3 grid(p.N / BN, ceil_div(p.M, BM * TM), p.splits);
     uint32_t* err = device_error_flag();
     if (p.pdl) {
         cudaLaunchConfig_t cfg = {};
@@ -669,20 +683,28 @@ pf_status launch_tc(const GemmParams& p, int plane_rows, cudaStream_t st) {
         at[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = at;
         cfg.numAttrs = 1;
-        PF_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, P, WF, EPI>, ta, tb, p, plane_rows, err));
+        PF_CUDA(cudaLaunchKernelEx(&cfg, gemm_tc_kernel<BN, P, WF, EPI, TM>, ta, tb, p, plane_rows, err));
     } else {
-        gemm_tc_kernel<BN, P, WF, EPI><<<grid, NUM_THREADS, Ly::SMEM, st>>>(ta, tb, p, plane_rows, err);
+        gemm_tc_kernel<BN, P, WF, EPI, TM><<<grid, NUM_THREADS, Ly::SMEM, st>>>(ta, tb, p, plane_rows, err);
     }
     return launch_check("gemm_tc");
 }
 
-template <int BN, int P, int EPI>
+template <int BN, int P, int EPI, int TM = 1>
 pf_status launch_wf(const GemmParams& p, int plane_rows, cudaStream_t st) {
     switch (p.wf) {
-        case WF_Q4: return launch_tc<BN, P, WF_Q4, EPI>(p, plane_rows, st);
-        case WF_Q2: return launch_tc<BN, P, WF_Q2, EPI>(p, plane_rows, st);
-        default: return launch_tc<BN, P, WF_I8, EPI>(p, plane_rows, st);
+        case WF_Q4: return launch_tc<BN, P, WF_Q4, EPI, TM>(p, plane_rows, st);
+        case WF_Q2: return launch_tc<BN, P, WF_Q2, EPI, TM>(p, plane_rows, st);
+        default: return launch_tc<BN, P, WF_I8, EPI, TM>(p, plane_rows, st);
     }
+}
+
+// Two 128-row M tiles per CTA (both accumulators in TMEM, each unpacked
+// weight stage feeding both): ~30% fewer shared-memory bytes per MMA, for
+// launches whose tile pairs still fill two waves (prefill-sized M).
+bool use_two_m_tiles(const GemmParams& p, int planes, int bn) {
+    return planes == 1 && bn == 256 && p.epi == EPI_SWIGLU && p.splits == 1 &&
+           (size_t)ceil_div(p.M, 2 * BM) * (p.N / bn) >= 2 * 148;
 }
 
 template <int BN>
@@ -703,7 +725,10 @@ pf_status launch_bn(const GemmParams& p, int planes, int plane_rows, cudaStream_
         case EPI_F32: return launch_wf<BN, 1, EPI_F32>(p, plane_rows, st);
         case EPI_QKV: return launch_wf<BN, 1, EPI_QKV>(p, plane_rows, st);
         case EPI_RESID: return launch_wf<BN, 1, EPI_RESID>(p, plane_rows, st);
-        default: return launch_wf<BN, 1, EPI_SWIGLU>(p, plane_rows, st);
+        default:
+            if constexpr (BN == 256)
+                if (use_two_m_tiles(p, planes, BN)) return launch_wf<BN, 1, EPI_SWIGLU, 2>(p, plane_rows, st);
+            return launch_wf<BN, 1, EPI_SWIGLU>(p, plane_rows, st);
     }
 }
 

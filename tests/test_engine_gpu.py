@@ -292,3 +292,20 @@ def test_generate_api(tiny):
         for b in range(2):
             want[b] += [int(t) for t in em[b, : n[b]]]
     assert out == [x[:12] for x in want]
+
+
+def test_prefill_two_m_tile_swiglu():
+    """Prefill chunks of 3,840 rows through a 5,120-column gate/up projection
+    run the SwiGLU GEMM with two 128-row M tiles per CTA (each unpacked
+    weight stage feeding both accumulators): prefill results, drafts, the
+    steps after them and the committed KV match the oracle.  One layer: with
+    two, this FFN (20 x d wide) grows the hidden state to ~1e6 and an int8
+    near-tie of the prefill reaches a later sequence's hidden state at ~1e-2
+    (the same with one M tile per CTA: the two forms are bit-identical).
+    (M = 64 x 60 = 3,840 rows, 20 column tiles of 256: 15 x 20 >= 2 x 148
+    tile pairs select the two-tile form.)"""
+    cfg = Cfg(n_layers=1, n_embd=128, n_heads=2, n_kv_heads=1, n_ff=2560, n_mtp_heads=2, max_context=1024)
+    w = make_weights(cfg, seed=7)
+    prm = prompts(64, 128, cfg.n_vocab, seed=11)
+    g, o = run_pair(cfg, w, prm, 2)
+    compare_kv(g, o, cfg, 64)
