@@ -521,7 +521,7 @@ pf_status pf_engine_create(const pf_model_config* c, int32_t max_seqs, int32_t m
     e->K = c->n_mtp_heads;
     e->R = e->K + 1;
     e->Mv = max_seqs * e->R;
-    e->Mcap = std::max(e->Mv, std::min(4096, max_seqs * 256));
+    e->Mcap = std::max(e->Mv, std::min(8192, max_seqs * 256));
     e->d = c->n_embd;
     e->H = c->n_heads;
     e->G = c->n_kv_heads;
