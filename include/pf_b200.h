@@ -246,6 +246,17 @@ PF_API pf_status pf_gemm_packed_static(const int8_t* Aq, const float* a_scale, c
  * mismatching bit pattern (0xFFFFFFFF if none). */
 PF_API pf_status pf_check_reciprocal(uint64_t* mismatches, uint32_t* first_bad);
 
+/* Diagnostic with no counterpart in the reference: checks, on the device, the
+ * one-warp exact form of the sampler's sequential float sums (the normalising
+ * sum and the cumulative scan) against the reference's one-at-a-time float
+ * loop.  terms: device [rows][n] (n <= 16384; terms >= 0, inf or NaN);
+ * sorted != 0: every row is non-increasing (the sorted rows' early exit is
+ * taken); u, p: device [rows], the scan stops at the first partial sum c with
+ * u <= c or c >= p.  *mismatches (host) receives the number of rows whose full
+ * sum, stop index or stopping sum differ in any bit. */
+PF_API pf_status pf_check_ordered_scan(const float* terms, int32_t rows, int32_t n, int32_t sorted, const float* u,
+                                       const float* p, uint32_t* mismatches);
+
 /* ------------------------------------------------------------------ */
 /* Engine: batched MTP speculative decoding                             */
 /* (Engine::generate / forward_with_hidden / MTPHeads::forward,         */

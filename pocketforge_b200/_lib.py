@@ -73,6 +73,7 @@ def lib():
     sig("pf_pack_weights", st, vp, i32, i32, i32, vp, vp)
     sig("pf_gemm_packed", st, vp, vp, vp, vp, i32, vp, i32, i32, i32, vp)
     sig("pf_check_reciprocal", st, vp, vp)
+    sig("pf_check_ordered_scan", st, vp, i32, i32, i32, vp, vp, vp)
     sig("pf_engine_create", st, C.POINTER(ModelConfigC), i32, i32, i32, C.POINTER(vp))
     sig("pf_engine_destroy", None, vp)
     sig("pf_engine_set_matrix", st, vp, i32, i32, vp, vp)

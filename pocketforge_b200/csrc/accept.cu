@@ -4,6 +4,7 @@
 // predictive FFN layer skipping, and the commit of per-sequence state.
 #include <cfloat>
 
+#include "scan.cuh"
 #include "step.cuh"
 
 namespace pf {
@@ -121,8 +122,9 @@ pf_status gather_rows(const float* x, int d, const int* idx, int n, float* out, 
 // memory.  The exponentials are computed in parallel (double exp rounded to
 // float: the correctly rounded value the reference's std::exp returns in all
 // but rare halfway cases) and so are the divisions by the sum; the
-// normalising sum and the cumulative scan are sequential float additions in
-// the reference's order, so the draw is the reference's.  One cumulative scan
+// normalising sum and the cumulative scan are the reference's sequential
+// float additions, reproduced exactly by one warp (ordered_scan_warp), so the
+// draw is the reference's.  One cumulative scan
 // finds both the draw and the top-p cut: the reference's two cumulative scans
 // add the same quotients in the same order, so their partial sums are the
 // same numbers, and whichever stops first decides the token.
@@ -386,72 +388,6 @@ __device__ __forceinline__ bool block_bucket_sort(uint32_t (&k)[SORT_IPT], uint3
     return true;
 }
 
-// One thread's cumulative float sum of a[0, n) in index order, continuing
-// from cum.  Returns the first i whose partial sum c satisfies stop(c) (cum is
-// then that sum), else n (cum is the full sum).  The terms are >= 0, so the
-// partial sums never decrease and stop (monotone in c) is checked once per 16
-// terms; only the group that holds the stop is added again, term by term.
-// The next 16 terms are loaded before the current 16 are added (a is 16-byte
-// aligned), so the loop runs at the latency of the dependent additions.
-// DESC: the terms never increase (sorted rows).  Then once a term is below a
-// quarter of the spacing of floats above the sum, every later term rounds
-// away (RN(c + q) = c for 0 <= q < ulp(c)/2; the factor 2 of margin covers a
-// term one float step above its predecessor, the double exp being within an
-// ulp but not guaranteed monotone): the sum is final and a stop that has not
-// held cannot start to, so the scan ends with the result of the full walk.
-__device__ __forceinline__ float quarter_ulp(float c) {  // c >= 0; 0 when too small to matter
-    const uint32_t e = __float_as_uint(c) >> 23;
-    return e >= 26 ? __uint_as_float((e - 25) << 23) : 0.0f;
-}
-template <bool DESC, typename Stop>
-__device__ __forceinline__ int ordered_scan(const float* a, int n, float& cum, Stop stop) {
-    const int n16 = n & ~15;
-    const float4* a4 = reinterpret_cast<const float4*>(a);
-    float4 q0 = make_float4(0.f, 0.f, 0.f, 0.f), q1 = q0, q2 = q0, q3 = q0;
-    if (n16 > 0) {
-        q0 = a4[0];
-        q1 = a4[1];
-        q2 = a4[2];
-        q3 = a4[3];
-    }
-    float c = cum;
-    for (int i = 0; i < n16; i += 16) {
-        const float4 t0 = q0, t1 = q1, t2 = q2, t3 = q3;
-        if (i + 16 < n16) {
-            q0 = a4[(i >> 2) + 4];
-            q1 = a4[(i >> 2) + 5];
-            q2 = a4[(i >> 2) + 6];
-            q3 = a4[(i >> 2) + 7];
-        }
-        const float c0 = c;
-        c = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(c, t0.x), t0.y), t0.z), t0.w);
-        c = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(c, t1.x), t1.y), t1.z), t1.w);
-        c = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(c, t2.x), t2.y), t2.z), t2.w);
-        c = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(c, t3.x), t3.y), t3.z), t3.w);
-        if (stop(c)) {
-            const float t[16] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w,
-                                 t2.x, t2.y, t2.z, t2.w, t3.x, t3.y, t3.z, t3.w};
-            float s = c0;
-            for (int j = 0; j < 16; j++) {
-                s = __fadd_rn(s, t[j]);
-                if (stop(s)) {
-                    cum = s;
-                    return i + j;
-                }
-            }
-        }
-        if (DESC && t3.w < quarter_ulp(c)) {
-            cum = c;
-            return n;
-        }
-    }
-    cum = c;
-    for (int i = n16; i < n; i++) {
-        cum = __fadd_rn(cum, a[i]);
-        if (stop(cum)) return i;
-    }
-    return n;
-}
 }  // namespace
 
 __global__ void __launch_bounds__(SORT_THREADS, 1)
@@ -488,19 +424,19 @@ __global__ void __launch_bounds__(SORT_THREADS, 1)
         mx = red[0];
         for (int i = tid; i < V; i += blockDim.x) key[i] = exp_ref(__fdiv_rn(__fsub_rn(lg[i], mx), t));
         __syncthreads();
-        if (tid == 0) {
+        if (tid < 32) {
             float sum = 0.0f;
-            ordered_scan<false>(key, V, sum, [](float) { return false; });
-            red[1] = sum;
+            ordered_scan_warp<false>(key, V, sum, [](float) { return false; });
+            if (tid == 0) red[1] = sum;
         }
         __syncthreads();
         const float sum = red[1];
         for (int i = tid; i < V; i += blockDim.x) key[i] = __fdiv_rn(key[i], sum);
         __syncthreads();
-        if (tid == 0) {
+        if (tid < 32) {
             float cum = 0.0f;
-            const int i = ordered_scan<false>(key, V, cum, [u](float c) { return u <= c; });
-            out[b] = i < V ? i : V - 1;
+            const int i = ordered_scan_warp<false>(key, V, cum, [u](float c) { return u <= c; });
+            if (tid == 0) out[b] = i < V ? i : V - 1;
         }
         return;
     }
@@ -524,17 +460,16 @@ __global__ void __launch_bounds__(SORT_THREADS, 1)
     // exponentials in sorted order, in place of the keys
     for (int i = tid; i < nn; i += blockDim.x) key[i] = exp_ref(__fdiv_rn(__fsub_rn(key_value(ks[i]), mx), t));
     __syncthreads();
-    if (tid == 0) {
-        // terms after the first zero are zero too (sorted descending) and add nothing
+    if (tid < 32) {
         float total = 0.0f;
-        ordered_scan<true>(key, nn, total, [](float) { return false; });
-        red[0] = total;
+        ordered_scan_warp<true>(key, nn, total, [](float) { return false; });
+        if (tid == 0) red[0] = total;
     }
     __syncthreads();
     const float total = red[0];
     for (int i = tid; i < nn; i += blockDim.x) key[i] = __fdiv_rn(key[i], total);  // the normalised terms
     __syncthreads();
-    if (tid != 0) return;
+    if (tid >= 32) return;
     float cum = 0.0f;
     int i;
     if (top_p) {
@@ -544,11 +479,11 @@ __global__ void __launch_bounds__(SORT_THREADS, 1)
         // entry by then takes the last kept one, entry i.  Either way the
         // token is the entry where the first of the two holds.
         const float p = cfg.top_p;
-        i = ordered_scan<true>(key, nn, cum, [u, p](float c) { return u <= c || c >= p; });
+        i = ordered_scan_warp<true>(key, nn, cum, [u, p](float c) { return u <= c || c >= p; });
     } else {  // top-k (src/engine.cpp:930-959)
-        i = ordered_scan<true>(key, nn, cum, [u](float c) { return u <= c; });
+        i = ordered_scan_warp<true>(key, nn, cum, [u](float c) { return u <= c; });
     }
-    out[b] = (int)vs[i < nn ? i : nn - 1];
+    if (tid == 0) out[b] = (int)vs[i < nn ? i : nn - 1];
 }
 
 pf_status sample_rows(const float* logits, int ld, int V, const int* rows, int n, const pf_sampling_config& cfg,

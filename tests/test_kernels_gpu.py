@@ -289,6 +289,78 @@ def test_empty_batches_are_noops():
     assert L.pf_gemm_packed(p(i8), p(f), p(packed), p(f), 1, p(f), 4, 64, 100, None) == 1  # K % 128 != 0
 
 
+def _scan_rows(rng, n):
+    """Rows of terms for the sampler's sums: exponentials of flat and steep
+    rows, values on a coarse grid (exact halfway cases everywhere), dyadic
+    values, zeros and tiny terms, terms of half an ulp of the running sum,
+    normalised quotients, plain uniforms."""
+    rows = []
+    for mode in range(8):
+        for _ in range(6):
+            U = rng.uniform(size=n)
+            spread = 10.0 ** rng.uniform(-1, 2)
+            if mode == 0:
+                z = np.exp(-spread * U)
+            elif mode == 1:
+                z = rng.integers(0, 64, n) * 0.125
+            elif mode == 2:
+                z = np.ldexp(rng.integers(0, 4096, n).astype(np.float64), -rng.integers(0, 30, n))
+            elif mode == 3:
+                z = np.where(U < 0.1, 0.0, np.exp(-30.0 * rng.uniform(size=n)))
+            elif mode == 4:
+                z = np.exp(-5.0 * spread * U) * 1e-6
+            elif mode == 5:
+                z = np.ldexp(1.0, -24 - rng.integers(0, 3, n)) * (1 + rng.integers(0, 3, n))
+                z[0] = 1.0
+            elif mode == 6:
+                z = np.exp(-spread * U)
+                z = z / z.sum()
+            else:
+                z = U
+            rows.append(z.astype(np.float32))
+    return np.stack(rows)
+
+
+def _scan_stops(rng, rows):
+    tot = rows.astype(np.float64).sum(axis=1)
+    us = (rng.uniform(size=len(rows)) * tot).astype(np.float32)
+    ps = ((0.5 + 0.5 * rng.uniform(size=len(rows))) * tot).astype(np.float32)
+    us[::7] = 0.0  # a draw of 0 stops at the first term
+    return us, ps
+
+
+@pytest.mark.parametrize("n", [16384, 5000, 37])
+def test_exact_warp_scan_matches_serial_float_sums(n):
+    """The sampler's normalising sum and cumulative scan are the reference's
+    one-at-a-time float additions (src/engine.cpp:895-1003); the kernel
+    computes them with one warp, exactly, from the rounding of each addition
+    within a binade of the running sum (scan.cuh).  The device compares that
+    with the plain float loop on every row: the full sum, the stop index and
+    the stopping sum must agree in every bit, in index order (unsorted rows:
+    temperature sampling) and on non-increasing rows (top-p / top-k, with the
+    early exit once terms fall below a quarter ulp of the sum)."""
+    rng = np.random.default_rng(n)
+    rows = _scan_rows(rng, n)
+    special = np.zeros((6, n), np.float32)
+    special[0] = 1.0
+    special[0, n // 3] = np.nan
+    special[1] = 0.5
+    special[1, n // 2] = np.inf
+    special[2] = np.float32(1e-40)  # subnormal terms: the float path
+    special[3] = np.float32(3e37)  # the sum overflows to inf
+    special[4, n // 2] = 1.0  # zeros, one term
+    special[5] = np.float32(2.0 ** -101)  # a sum that starts below 2^-100 and grows past it
+    unsorted = np.concatenate([rows, special])
+    us, ps = _scan_stops(rng, unsorted)
+    us[len(rows):] = [0.3, 0.9, 1e-38, 1e38, 0.5, 1e-30]
+    ps[len(rows):] = [0.9, 0.9, 1e-37, np.inf, 0.9, 1e-29]
+    for terms, sorted_, uu, pp in ((unsorted, 0, us, ps), (-np.sort(-rows, axis=1), 1) + _scan_stops(rng, rows)):
+        bad = C.c_uint32(0)
+        _lib.check(_lib.lib().pf_check_ordered_scan(p(dev(terms)), len(terms), n, sorted_, p(dev(uu)), p(dev(pp)),
+                                                    C.byref(bad)), "pf_check_ordered_scan")
+        assert bad.value == 0, f"{bad.value} of {len(terms)} rows differ (sorted={sorted_})"
+
+
 def test_branch_free_reciprocal_is_correctly_rounded():
     """The SwiGLU epilogues take 1 / (1 + exp(-g)) from a branch-free double
     Newton iteration (numerics.cuh) so that many of them interleave; it must
