@@ -25,7 +25,8 @@ namespace pf {
 // (after a map with beta != 0 the parity of R is that of alpha, whatever R
 // was).  A window of 512 terms is 16 consecutive terms per lane: each lane
 // composes its own, a warp scan composes the lanes, and every partial sum of
-// the window follows exactly.  The first addition whose sum would leave the
+// the window follows exactly; the lane whose run holds the first event walks
+// it term by term.  The first addition whose sum would leave the
 // binade (or whose term is not finite) is done as a float addition, and the
 // next window starts after it.  While the sum is zero, below 2^-100 or not
 // finite, lane 0 adds the terms one at a time (as the reference does), and a
@@ -129,46 +130,57 @@ __device__ __forceinline__ int ordered_scan_warp(const float* a, int n, float& c
             t[4 * q + 2] = v.z;
             t[4 * q + 3] = v.w;
         }
-        GridMap agg{0, 0};
 #pragma unroll
-        for (int j = 0; j < kWinPer; j++) {
+        for (int j = 0; j < kWinPer; j++)
             if (base + j < pos) t[j] = 0.0f;
-            agg = map_then(agg, map_of(t[j], mult));
-        }
-        GridMap inc = agg;  // lanes 0 .. lane
+        // this lane's 16 maps composed as a tree (depth 4, not a chain of 16)
+        GridMap m[kWinPer];
+#pragma unroll
+        for (int j = 0; j < kWinPer; j++) m[j] = map_of(t[j], mult);
+#pragma unroll
+        for (int s = 1; s < kWinPer; s <<= 1)
+#pragma unroll
+            for (int j = 0; j + s < kWinPer; j += 2 * s) m[j] = map_then(m[j], m[j + s]);
+        GridMap inc = m[0];  // lanes 0 .. lane
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const GridMap y{__shfl_up_sync(FULL, inc.a, o), __shfl_up_sync(FULL, inc.b, o)};
             if (lane >= o) inc = map_then(y, inc);
         }
-        GridMap exc{__shfl_up_sync(FULL, inc.a, 1), __shfl_up_sync(FULL, inc.b, 1)};
-        if (lane == 0) exc = GridMap{0, 0};
-        // this lane's partial sums: the first that leaves the binade or stops
-        int r = map_apply(exc, R);
-        int ev = kWinPer, rev = 0, evstop = 0;
-#pragma unroll
-        for (int j = 0; j < kWinPer; j++) {
-            if (ev == kWinPer) {
-                const int rn = map_apply(map_of(t[j], mult), r);
-                if (rn >= (1 << 24)) {
-                    ev = j;
-                    rev = r;
-                } else if (stop(__fmul_rn(__int2float_rn(rn), g))) {
-                    ev = j;
-                    rev = rn;
-                    evstop = 1;
-                }
-                r = rn;
-            }
-        }
-        const unsigned hit = __ballot_sync(FULL, ev < kWinPer);
+        // R and stop are monotone along the window: a lane's run holds the
+        // first event (an addition leaving the binade, or the stop) if its
+        // last partial sum has one and no earlier lane's does.
+        const int r_end = map_apply(inc, R);
+        const unsigned hit =
+            __ballot_sync(FULL, r_end >= (1 << 24) || stop(__fmul_rn(__int2float_rn(r_end), g)));
         if (hit == 0) {
-            const GridMap all{__shfl_sync(FULL, inc.a, 31), __shfl_sync(FULL, inc.b, 31)};
-            c = __fmul_rn(__int2float_rn(map_apply(all, R)), g);
+            c = __fmul_rn(__int2float_rn(__shfl_sync(FULL, r_end, 31)), g);
             pos = ws + 32 * kWinPer;
             continue;
         }
         const int src = __ffs(hit) - 1;
+        GridMap exc{__shfl_up_sync(FULL, inc.a, 1), __shfl_up_sync(FULL, inc.b, 1)};
+        if (lane == 0) exc = GridMap{0, 0};
+        // lane src walks its run to the event
+        int ev = kWinPer, rev = 0, evstop = 0;
+        if (lane == src) {
+            int r = map_apply(exc, R);
+#pragma unroll
+            for (int j = 0; j < kWinPer; j++) {
+                if (ev == kWinPer) {
+                    const int rn = map_apply(map_of(t[j], mult), r);
+                    if (rn >= (1 << 24)) {
+                        ev = j;
+                        rev = r;
+                    } else if (stop(__fmul_rn(__int2float_rn(rn), g))) {
+                        ev = j;
+                        rev = rn;
+                        evstop = 1;
+                    }
+                    r = rn;
+                }
+            }
+        }
         const int i = ws + kWinPer * src + __shfl_sync(FULL, ev, src);
         const float cb = __fmul_rn(__int2float_rn(__shfl_sync(FULL, rev, src)), g);
         if (__shfl_sync(FULL, evstop, src)) {
